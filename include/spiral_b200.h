@@ -1,0 +1,208 @@
+/*
+ * spiral_b200.h — C-ABI of the B200 (sm_100a) quantized-weight library.
+ *
+ * The library dequantizes canonical GGUF Q4_0, Q8_0 and Q6_K weights to bf16
+ * and runs the quantized MUL_MAT (quantized src0 x bf16 src1) that consumes
+ * them, on NVIDIA B200 GPUs.  Everything here is plain C: pointers, sizes,
+ * integer enums.  Device pointers are CUDA device (or managed) pointers; a
+ * `stream` argument is a cudaStream_t passed as `void*` (NULL = legacy default
+ * stream).  Calls are stream-ordered and return as soon as the work is queued.
+ *
+ * Naming follows the reference's weight-matrix vocabulary
+ * (spiral src/quants/TODO.md:246-266):
+ *   weights_rows = K  (reduction length, = inputs_len)
+ *   weights_cols = N  (output features, = outputs_len)
+ *   inputs_vecs  = M  (number of activation vectors)
+ * GGUF stores the weight matrix "column-major" in that vocabulary: each of
+ * the N output features holds its K weights as consecutive blocks.  In ggml
+ * terms that is src0 with ne0 = K, ne1 = N, one row per output feature.
+ *
+ * Numerics (all formats): a weight is fp16 scale x integer, computed exactly
+ * in fp32 and rounded once to bf16 round-to-nearest-even.  This equals the
+ * reference oracle (src/quants/tests/formats/q4_0.py:42-62, q8_0.py:43-60,
+ * q6_k.py:55-112, cast with ml_dtypes bfloat16) bit for bit.  Subnormal fp16
+ * scales are decoded exactly by default (GGUF semantics); SPIRAL_FLAG_FTZ_SCALES
+ * flushes them to +0 as the reference NPU device path does
+ * (src/quants/common/repack.h:29-34, common/scale.aie.h:9-13).
+ *
+ * Errors: every int-returning call returns SPIRAL_OK (0) or a negative
+ * spiral_status.  Size queries and the repack return 0 on invalid input,
+ * exactly like the reference's record_count / packed_bytes / repack_weights
+ * (src/quants/q4_0/repack.h:10-41, TODO.md:331-334).  Nothing throws or traps.
+ */
+#ifndef SPIRAL_B200_H
+#define SPIRAL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SPIRAL_API __attribute__((visibility("default")))
+#else
+#define SPIRAL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Quantized formats.  The values are ggml's `enum ggml_type` ids, so a ggml
+ * backend can pass src0->type straight through. */
+typedef enum spiral_qfmt {
+  SPIRAL_QFMT_Q4_0 = 2,  /* 18-byte block: fp16 d, 16 B nibbles; w=(q-8)*d   */
+  SPIRAL_QFMT_Q8_0 = 8,  /* 34-byte block: fp16 d, 32 int8;      w=q*d       */
+  SPIRAL_QFMT_Q6_K = 14  /* 210-byte super-block of 256: ql[128] qh[64]
+                            sc[16] d; w=d*sc*(q-32)                          */
+} spiral_qfmt;
+
+/* Output element types (ggml type ids). */
+typedef enum spiral_dtype {
+  SPIRAL_DTYPE_F32 = 0,
+  SPIRAL_DTYPE_BF16 = 30
+} spiral_dtype;
+
+typedef enum spiral_status {
+  SPIRAL_OK = 0,
+  SPIRAL_ERR_INVALID_FORMAT = -1,  /* fmt is not one of spiral_qfmt          */
+  SPIRAL_ERR_INVALID_SHAPE = -2,   /* non-positive dims, K not a block multiple,
+                                      stride smaller than a row               */
+  SPIRAL_ERR_NULL_POINTER = -3,
+  SPIRAL_ERR_ALIGNMENT = -4,       /* pointer/stride alignment the op needs   */
+  SPIRAL_ERR_CAPACITY = -5,        /* caller buffer or workspace too small    */
+  SPIRAL_ERR_CUDA = -6,            /* a CUDA runtime call failed              */
+  SPIRAL_ERR_NCCL = -7,            /* a NCCL call failed                      */
+  SPIRAL_ERR_TIMEOUT = -8,         /* a bounded device or host wait gave up   */
+  SPIRAL_ERR_UNSUPPORTED = -9,     /* valid request this build cannot serve   */
+  SPIRAL_ERR_INVALID_ARGUMENT = -10
+} spiral_status;
+
+/* Flags (bit set). */
+#define SPIRAL_FLAG_FTZ_SCALES 0x1u  /* flush subnormal fp16 scales to +0      */
+#define SPIRAL_FLAG_ACCUMULATE 0x2u  /* mul_mat: dst += result (f32 dst only)  */
+
+/* ---------------------------------------------------------------- info --- */
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+SPIRAL_API int spiral_version(void);
+
+/* Static text for a status code. */
+SPIRAL_API const char* spiral_status_string(int status);
+
+/* Detail text of the last error raised on the calling host thread ("" when
+ * none).  Valid until the next library call on the same thread. */
+SPIRAL_API const char* spiral_last_error(void);
+
+/* Synchronizes `stream`, then reads and clears the device-side error word of
+ * the current device into *code.  Kernels never trap: a bounded wait (an
+ * mbarrier or peer flag) that gives up sets a bit (1 = pipeline wait timeout,
+ * 2 = tensor-memory allocation failure, 4 = bad launch geometry) and the
+ * kernel ends early.  Returns SPIRAL_ERR_TIMEOUT when any bit was set.
+ * No reference counterpart: the reference's only device watchdog is the XRT
+ * run.wait2(5000 ms) host timeout (tests/poc/invoke.cc:25-26, 126-131). */
+SPIRAL_API int spiral_device_status(void* stream, uint32_t* code);
+
+/* Weights per block (32, 32, 256) and bytes per block (18, 34, 210); 0 for an
+ * unknown format.  Mirrors the per-format kBlockRows / kBlockBytes constants
+ * of src/quants/<fmt>/layout.h (q4_0/layout.h:10-12, q8_0/layout.h:10-13,
+ * q6_k/layout.h:10-15). */
+SPIRAL_API int64_t spiral_quants_block_rows(int fmt);
+SPIRAL_API int64_t spiral_quants_block_bytes(int fmt);
+
+/* ------------------------------------------------- size queries / repack -- */
+
+/* Number of canonical blocks of a weights_rows x weights_cols tensor, or 0 if
+ * the shape is invalid (non-positive, or weights_rows not a multiple of the
+ * block's weight count).
+ * Replaces: extern "C" int64_t quants_record_count(rows, cols)
+ *           (src/quants/tests/repack.cc:13-16).  The reference counts NPU
+ *           records; the B200 kernels read canonical GGUF blocks directly, so
+ *           the record here is the canonical block. */
+SPIRAL_API int64_t spiral_quants_record_count(int fmt, int64_t weights_rows,
+                                   int64_t weights_cols);
+
+/* Dense canonical bytes of the tensor (record_count * block bytes), 0 if
+ * invalid.
+ * Replaces: extern "C" int64_t quants_packed_bytes(rows, cols)
+ *           (src/quants/tests/repack.cc:18-21). */
+SPIRAL_API int64_t spiral_quants_packed_bytes(int fmt, int64_t weights_rows,
+                                   int64_t weights_cols);
+
+/* Device-side repack of a (possibly padded) canonical tensor view into the
+ * dense device layout every kernel here reads: weights_cols rows of
+ * packed_bytes/weights_cols bytes.  `src` and `dst` are device pointers;
+ * src_col_stride_bytes >= the dense row size.  Returns bytes written, or 0 on
+ * invalid dims, insufficient capacity, null pointers or a CUDA error.
+ * Replaces: extern "C" int64_t quants_repack(src, src_col_stride_bytes, dst,
+ *           dst_capacity, rows, cols) (src/quants/tests/repack.cc:23-32,
+ *           q4_0/repack.h:27-41).  Same argument meaning and return contract;
+ *           the destination layout is canonical GGUF instead of NPU records. */
+SPIRAL_API int64_t spiral_quants_repack(int fmt, const void* src,
+                             int64_t src_col_stride_bytes, void* dst,
+                             int64_t dst_capacity, int64_t weights_rows,
+                             int64_t weights_cols, void* stream);
+
+/* ------------------------------------------------------ dequant-to-bf16 -- */
+
+/* ggml-style dequantize (to_float / dequantize_row_* semantics):
+ *   dst[n * dst_row_stride_elems + k] = bf16(W[n][k]),  n < N, k < K
+ * src: device pointer to N rows of K/blk canonical blocks, row n at
+ * src + n * src_row_stride_bytes.  dst: device bf16 (uint16_t) buffer.
+ * Bit-exact against the reference oracle (see header comment).
+ * Fast path: 16-byte aligned src/dst, 16-byte multiple strides and
+ * K % 256 == 0 (Q4_0/Q8_0) or K % 2048 == 0 (Q6_K); other valid shapes run a
+ * slower scalar-load kernel with the same results. */
+SPIRAL_API int spiral_dequant_bf16(int fmt, const void* src, int64_t src_row_stride_bytes,
+                        void* dst, int64_t dst_row_stride_elems, int64_t K,
+                        int64_t N, unsigned flags, void* stream);
+
+/* Dequantize a dense canonical tensor into the reference's bf16 weights
+ * stream order [weights_cols/8][weights_rows][8] (the order of
+ * formats/<fmt>.py reference_weights: [cols_tile][rows_record][chunk]
+ * [kUnpackTileRows][kTileCols], which flattens to [cols/8][rows][8]).
+ * weights_cols must be a multiple of 8 (kTileCols).
+ * Replaces: extern "C" void quants_unpack_all(const uint8_t* packed,
+ *           bfloat16* out) (src/quants/tests/unpack.aie.cc:21-45), whose
+ *           format and shape are compile-time macros there and arguments here.
+ */
+SPIRAL_API int spiral_quants_unpack_all(int fmt, const void* packed, void* weights_bf16,
+                             int64_t weights_rows, int64_t weights_cols,
+                             unsigned flags, void* stream);
+
+/* ------------------------------------------------------------ MUL_MAT ---- */
+
+/* ggml MUL_MAT with a quantized src0 and a bf16 src1:
+ *   y[m][n] = sum_k bf16(W[n][k]) * x[m][k],   m < M, n < N
+ * accumulated in fp32 and stored as y_dtype (BF16 rounds once, RNE; F32 with
+ * SPIRAL_FLAG_ACCUMULATE adds into y).
+ * w: N rows of canonical blocks at w_row_stride_bytes; x: M rows of K bf16 at
+ * x_row_stride_elems; y: M rows of N at y_row_stride_elems.
+ * M <= 8 runs the fused dequant-GEMV (decode); larger M runs the tcgen05
+ * dequant-GEMM (prefill).  Results are within fp32-summation-order error of
+ * the reference's dequant-then-fp32-matmul (src/quants/tests/mmul.py:104-121).
+ */
+SPIRAL_API int spiral_mul_mat(int fmt, const void* w, int64_t w_row_stride_bytes,
+                   const void* x, int64_t x_row_stride_elems, void* y,
+                   int y_dtype, int64_t y_row_stride_elems, int64_t M,
+                   int64_t N, int64_t K, unsigned flags, void* stream);
+
+/* Fused unpack + mmul in the reference's tiled I/O orders:
+ *   inputs  bf16 [weights_rows/8][inputs_vecs][8]
+ *   outputs f32  [weights_cols/8][inputs_vecs][8], ACCUMULATED (+=); the
+ *           caller zeroes them, as the reference shim does.
+ * weights: dense canonical tensor.  weights_rows % 8 == 0 and
+ * weights_cols % 8 == 0 are required by the tiled orders.
+ * Replaces: extern "C" void quants_unpack_mmul_all(const uint8_t* packed,
+ *           const bfloat16* inputs, float* outputs)
+ *           (src/quants/tests/mmul.aie.cc:20-35; layouts mmul.py:22-35,
+ *           113-118), with format/shape as arguments instead of macros. */
+SPIRAL_API int spiral_quants_unpack_mmul_all(int fmt, const void* packed,
+                                  const void* inputs_bf16, float* outputs,
+                                  int64_t weights_rows, int64_t weights_cols,
+                                  int64_t inputs_vecs, unsigned flags,
+                                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPIRAL_B200_H */

@@ -1,0 +1,190 @@
+"""spiral_b200 — B200-native GGUF dequant / quantized MUL_MAT.
+
+Python mirror of the C-ABI in include/spiral_b200.h (loaded with ctypes, the
+way the reference's harness loads its host shim: src/quants/tests/common.py
+:308-341).  The compute runs in libspiral_b200.so (hand-written sm_100a CUDA);
+there is no Python or CPU fallback: if the library is missing, every entry
+point raises.
+
+Tensors may be torch CUDA tensors or raw device pointers (ints).  Shapes use
+ggml's convention: a quantized weight has N rows (output features) of K
+weights; activations are [M][K]; outputs [M][N].
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libspiral_b200.so"
+
+Q4_0, Q8_0, Q6_K = 2, 8, 14
+F32, BF16 = 0, 30
+FLAG_FTZ_SCALES = 0x1
+FLAG_ACCUMULATE = 0x2
+FORMATS = {"q4_0": Q4_0, "q8_0": Q8_0, "q6_k": Q6_K}
+BLOCK_K = {Q4_0: 32, Q8_0: 32, Q6_K: 256}
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q6_K: 210}
+
+# Every symbol include/spiral_b200.h declares, with (argtypes, restype).
+_i64, _i32, _vp, _u32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_uint
+_SIGNATURES = {
+    "spiral_version": ([], _i32),
+    "spiral_status_string": ([_i32], ctypes.c_char_p),
+    "spiral_last_error": ([], ctypes.c_char_p),
+    "spiral_device_status": ([_vp, ctypes.POINTER(ctypes.c_uint32)], _i32),
+    "spiral_quants_block_rows": ([_i32], _i64),
+    "spiral_quants_block_bytes": ([_i32], _i64),
+    "spiral_quants_record_count": ([_i32, _i64, _i64], _i64),
+    "spiral_quants_packed_bytes": ([_i32, _i64, _i64], _i64),
+    "spiral_quants_repack": ([_i32, _vp, _i64, _vp, _i64, _i64, _i64, _vp], _i64),
+    "spiral_dequant_bf16": ([_i32, _vp, _i64, _vp, _i64, _i64, _i64, _u32, _vp], _i32),
+    "spiral_quants_unpack_all": ([_i32, _vp, _vp, _i64, _i64, _u32, _vp], _i32),
+    "spiral_mul_mat": ([_i32, _vp, _i64, _vp, _i64, _vp, _i32, _i64, _i64, _i64, _i64, _u32, _vp], _i32),
+    "spiral_quants_unpack_mmul_all": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _u32, _vp], _i32),
+}
+
+_lib = None
+
+
+class SpiralError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"spiral status {status}: {message}")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded C-ABI library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m spiral_b200.build` "
+                "(this package has no CPU fallback)"
+            )
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (args, res) in _SIGNATURES.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = res
+        _lib = L
+    return _lib
+
+
+def fmt_id(fmt) -> int:
+    return FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        msg = lib().spiral_last_error().decode() or lib().spiral_status_string(status).decode()
+        raise SpiralError(status, msg)
+
+
+def _ptr(t) -> int:
+    if t is None:
+        return 0
+    if isinstance(t, int):
+        return t
+    return int(t.data_ptr())
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        try:
+            import torch
+
+            if torch.cuda.is_available():
+                return int(torch.cuda.current_stream().cuda_stream)
+        except Exception:
+            pass
+        return 0
+    if isinstance(stream, int):
+        return stream
+    return int(stream.cuda_stream)
+
+
+# ------------------------------------------------------------ size queries
+
+
+def record_count(fmt, weights_rows: int, weights_cols: int) -> int:
+    return lib().spiral_quants_record_count(fmt_id(fmt), weights_rows, weights_cols)
+
+
+def packed_bytes(fmt, weights_rows: int, weights_cols: int) -> int:
+    return lib().spiral_quants_packed_bytes(fmt_id(fmt), weights_rows, weights_cols)
+
+
+def row_bytes(fmt, K: int) -> int:
+    f = fmt_id(fmt)
+    return (K // BLOCK_K[f]) * BLOCK_BYTES[f]
+
+
+def repack(fmt, src, src_col_stride_bytes: int, dst, dst_capacity: int, weights_rows: int, weights_cols: int,
+           stream=None) -> int:
+    """Bytes written, 0 on invalid input (reference repack contract)."""
+    return lib().spiral_quants_repack(fmt_id(fmt), _ptr(src), src_col_stride_bytes, _ptr(dst), dst_capacity,
+                                      weights_rows, weights_cols, _stream(stream))
+
+
+def device_status(stream=None) -> int:
+    code = ctypes.c_uint32(0)
+    st = lib().spiral_device_status(_stream(stream), ctypes.byref(code))
+    if st not in (0, -8):
+        _check(st)
+    return code.value
+
+
+# ------------------------------------------------------------------ ops
+
+
+def dequant_bf16(fmt, w, K: int, N: int, out=None, *, w_row_stride: int | None = None,
+                 out_row_stride: int | None = None, ftz: bool = False, stream=None):
+    """ggml-style dequantize: out[n][k] = bf16(W[n][k])."""
+    f = fmt_id(fmt)
+    if out is None:
+        import torch
+
+        out = torch.empty((N, K), dtype=torch.bfloat16, device=w.device)
+    _check(lib().spiral_dequant_bf16(f, _ptr(w), w_row_stride or row_bytes(f, K), _ptr(out), out_row_stride or K,
+                                     K, N, FLAG_FTZ_SCALES if ftz else 0, _stream(stream)))
+    return out
+
+
+def unpack_all(fmt, packed, weights_rows: int, weights_cols: int, out=None, *, ftz: bool = False, stream=None):
+    """Reference-order dequant: out = [weights_cols/8][weights_rows][8] bf16."""
+    f = fmt_id(fmt)
+    if out is None:
+        import torch
+
+        out = torch.empty((weights_rows * weights_cols,), dtype=torch.bfloat16, device=packed.device)
+    _check(lib().spiral_quants_unpack_all(f, _ptr(packed), _ptr(out), weights_rows, weights_cols,
+                                          FLAG_FTZ_SCALES if ftz else 0, _stream(stream)))
+    return out
+
+
+def mul_mat(fmt, w, x, N: int, K: int, y=None, *, y_dtype: int = BF16, w_row_stride: int | None = None,
+            x_row_stride: int | None = None, y_row_stride: int | None = None, accumulate: bool = False,
+            ftz: bool = False, stream=None, M: int | None = None):
+    """ggml MUL_MAT: y[m][n] = sum_k bf16(W[n][k]) * x[m][k] (fp32 accumulate)."""
+    f = fmt_id(fmt)
+    if M is None:
+        M = int(x.shape[0])
+    if y is None:
+        import torch
+
+        y = torch.empty((M, N), dtype=torch.bfloat16 if y_dtype == BF16 else torch.float32, device=x.device)
+    flags = (FLAG_FTZ_SCALES if ftz else 0) | (FLAG_ACCUMULATE if accumulate else 0)
+    _check(lib().spiral_mul_mat(f, _ptr(w), w_row_stride or row_bytes(f, K), _ptr(x), x_row_stride or K, _ptr(y),
+                                y_dtype, y_row_stride or N, M, N, K, flags, _stream(stream)))
+    return y
+
+
+def unpack_mmul_all(fmt, packed, inputs_tiled, outputs, weights_rows: int, weights_cols: int, inputs_vecs: int, *,
+                    ftz: bool = False, stream=None):
+    """Reference fused op: outputs[N/8][M][8] (f32) += unpack(W) x inputs[K/8][M][8]."""
+    _check(lib().spiral_quants_unpack_mmul_all(fmt_id(fmt), _ptr(packed), _ptr(inputs_tiled), _ptr(outputs),
+                                               weights_rows, weights_cols, inputs_vecs,
+                                               FLAG_FTZ_SCALES if ftz else 0, _stream(stream)))
+    return outputs

@@ -1,0 +1,309 @@
+// api.cu — the extern "C" boundary of libspiral_b200.so.
+//
+// Host code is plain C-style: every entry point validates its arguments,
+// picks a kernel, queues it on the caller's stream and returns a status.
+// There is no host-side fallback: if a kernel cannot be launched the call
+// fails with SPIRAL_ERR_CUDA and a message from spiral_last_error().
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/spiral_b200.h"
+#include "api_internal.h"
+#include "common.cuh"
+
+namespace spiral {
+
+__device__ uint32_t g_device_error = 0;
+
+namespace {
+
+thread_local char g_last_error[512] = {0};
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(SPIRAL_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool fmt_valid(int fmt) { return fmt == kQ4_0 || fmt == kQ8_0 || fmt == kQ6_K; }
+
+int64_t block_k(int fmt) {
+  switch (fmt) {
+    case kQ4_0: return 32;
+    case kQ8_0: return 32;
+    case kQ6_K: return 256;
+  }
+  return 0;
+}
+int64_t block_bytes(int fmt) {
+  switch (fmt) {
+    case kQ4_0: return 18;
+    case kQ8_0: return 34;
+    case kQ6_K: return 210;
+  }
+  return 0;
+}
+
+int64_t row_bytes(int fmt, int64_t K) { return (K / block_k(fmt)) * block_bytes(fmt); }
+
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_sm_count[kMaxDevices];
+std::atomic<int> g_smem_optin[kMaxDevices];
+
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+  return dev;
+}
+
+int check_shape(int fmt, int64_t K, int64_t N) {
+  if (!fmt_valid(fmt)) return fail(SPIRAL_ERR_INVALID_FORMAT, "unknown quantized format %d", fmt);
+  if (K <= 0 || N <= 0) return fail(SPIRAL_ERR_INVALID_SHAPE, "dims must be positive (K=%lld N=%lld)", (long long)K,
+                                    (long long)N);
+  if (K % block_k(fmt) != 0)
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "K=%lld is not a multiple of the block size %lld", (long long)K,
+                (long long)block_k(fmt));
+  return SPIRAL_OK;
+}
+
+}  // namespace
+
+int device_sm_count() {
+  const int dev = current_device();
+  int v = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (v <= 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    g_sm_count[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
+size_t device_max_smem_optin() {
+  const int dev = current_device();
+  int v = g_smem_optin[dev].load(std::memory_order_relaxed);
+  if (v <= 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0)
+      v = 232448;
+    g_smem_optin[dev].store(v, std::memory_order_relaxed);
+  }
+  return static_cast<size_t>(v);
+}
+
+}  // namespace spiral
+
+using namespace spiral;
+
+extern "C" {
+
+int spiral_version(void) { return 100; }
+
+const char* spiral_status_string(int status) {
+  switch (status) {
+    case SPIRAL_OK: return "ok";
+    case SPIRAL_ERR_INVALID_FORMAT: return "invalid format";
+    case SPIRAL_ERR_INVALID_SHAPE: return "invalid shape";
+    case SPIRAL_ERR_NULL_POINTER: return "null pointer";
+    case SPIRAL_ERR_ALIGNMENT: return "misaligned pointer or stride";
+    case SPIRAL_ERR_CAPACITY: return "buffer too small";
+    case SPIRAL_ERR_CUDA: return "CUDA error";
+    case SPIRAL_ERR_NCCL: return "NCCL error";
+    case SPIRAL_ERR_TIMEOUT: return "timeout";
+    case SPIRAL_ERR_UNSUPPORTED: return "unsupported";
+    case SPIRAL_ERR_INVALID_ARGUMENT: return "invalid argument";
+  }
+  return "unknown status";
+}
+
+const char* spiral_last_error(void) { return g_last_error; }
+
+int64_t spiral_quants_block_rows(int fmt) { return fmt_valid(fmt) ? block_k(fmt) : 0; }
+int64_t spiral_quants_block_bytes(int fmt) { return fmt_valid(fmt) ? block_bytes(fmt) : 0; }
+
+int64_t spiral_quants_record_count(int fmt, int64_t weights_rows, int64_t weights_cols) {
+  if (!fmt_valid(fmt) || weights_rows <= 0 || weights_cols <= 0 || weights_rows % block_k(fmt) != 0) return 0;
+  return (weights_rows / block_k(fmt)) * weights_cols;
+}
+
+int64_t spiral_quants_packed_bytes(int fmt, int64_t weights_rows, int64_t weights_cols) {
+  return spiral_quants_record_count(fmt, weights_rows, weights_cols) * (fmt_valid(fmt) ? block_bytes(fmt) : 0);
+}
+
+int64_t spiral_quants_repack(int fmt, const void* src, int64_t src_col_stride_bytes, void* dst, int64_t dst_capacity,
+                             int64_t weights_rows, int64_t weights_cols, void* stream) {
+  g_last_error[0] = 0;
+  const int64_t bytes = spiral_quants_packed_bytes(fmt, weights_rows, weights_cols);
+  if (bytes == 0 || src == nullptr || dst == nullptr || bytes > dst_capacity) return 0;
+  const int64_t rb = row_bytes(fmt, weights_rows);
+  if (src_col_stride_bytes < rb) return 0;
+  const cudaError_t e =
+      cudaMemcpy2DAsync(dst, static_cast<size_t>(rb), src, static_cast<size_t>(src_col_stride_bytes),
+                        static_cast<size_t>(rb), static_cast<size_t>(weights_cols), cudaMemcpyDefault,
+                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    cuda_fail(e, "repack copy");
+    return 0;
+  }
+  return bytes;
+}
+
+int spiral_dequant_bf16(int fmt, const void* src, int64_t src_row_stride_bytes, void* dst,
+                        int64_t dst_row_stride_elems, int64_t K, int64_t N, unsigned flags, void* stream) {
+  g_last_error[0] = 0;
+  if (int st = check_shape(fmt, K, N)) return st;
+  if (src == nullptr || dst == nullptr) return fail(SPIRAL_ERR_NULL_POINTER, "null src or dst");
+  if (src_row_stride_bytes < row_bytes(fmt, K))
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "src row stride %lld < row bytes %lld", (long long)src_row_stride_bytes,
+                (long long)row_bytes(fmt, K));
+  if (dst_row_stride_elems < K)
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "dst row stride %lld < K %lld", (long long)dst_row_stride_elems,
+                (long long)K);
+  if ((reinterpret_cast<uintptr_t>(src) & 1u) || (src_row_stride_bytes & 1) || (reinterpret_cast<uintptr_t>(dst) & 1u))
+    return fail(SPIRAL_ERR_ALIGNMENT, "src/dst and the src row stride must be 2-byte aligned");
+  const cudaError_t e = dequant_rows(fmt, src, src_row_stride_bytes, dst, dst_row_stride_elems, K, N,
+                                     (flags & SPIRAL_FLAG_FTZ_SCALES) != 0, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dequant launch");
+  return SPIRAL_OK;
+}
+
+int spiral_quants_unpack_all(int fmt, const void* packed, void* weights_bf16, int64_t weights_rows,
+                             int64_t weights_cols, unsigned flags, void* stream) {
+  g_last_error[0] = 0;
+  if (int st = check_shape(fmt, weights_rows, weights_cols)) return st;
+  if (weights_cols % 8 != 0)
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "weights_cols=%lld must be a multiple of 8", (long long)weights_cols);
+  if (packed == nullptr || weights_bf16 == nullptr) return fail(SPIRAL_ERR_NULL_POINTER, "null packed or output");
+  if ((reinterpret_cast<uintptr_t>(packed) & 1u) || (reinterpret_cast<uintptr_t>(weights_bf16) & 15u))
+    return fail(SPIRAL_ERR_ALIGNMENT, "packed must be 2-byte and output 16-byte aligned");
+  const cudaError_t e = dequant_tiles_ref(fmt, packed, row_bytes(fmt, weights_rows), weights_bf16, weights_rows,
+                                          weights_cols, (flags & SPIRAL_FLAG_FTZ_SCALES) != 0,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "unpack_all launch");
+  return SPIRAL_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Runs y = x W^T for any M by slicing the activation vectors into batches of
+// at most 8 for the GEMV kernel.  (Large M is served by the GEMM kernel once
+// it is selected by spiral_mul_mat.)
+int run_mat(MatArgs a, cudaStream_t stream) {
+  const int64_t M = a.M;
+  for (int64_t m0 = 0; m0 < M; m0 += 8) {
+    MatArgs b = a;
+    b.M = std::min<int64_t>(8, M - m0);
+    b.x = a.x + m0 * a.x_sm;
+    if (a.y_bf16)
+      b.y = static_cast<uint16_t*>(a.y) + m0 * a.y_sm;
+    else
+      b.y = static_cast<float*>(a.y) + m0 * a.y_sm;
+    const cudaError_t e = gemv(b, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+  }
+  return SPIRAL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int spiral_mul_mat(int fmt, const void* w, int64_t w_row_stride_bytes, const void* x, int64_t x_row_stride_elems,
+                   void* y, int y_dtype, int64_t y_row_stride_elems, int64_t M, int64_t N, int64_t K, unsigned flags,
+                   void* stream) {
+  g_last_error[0] = 0;
+  if (int st = check_shape(fmt, K, N)) return st;
+  if (M <= 0) return fail(SPIRAL_ERR_INVALID_SHAPE, "M=%lld must be positive", (long long)M);
+  if (w == nullptr || x == nullptr || y == nullptr) return fail(SPIRAL_ERR_NULL_POINTER, "null w, x or y");
+  if (y_dtype != SPIRAL_DTYPE_BF16 && y_dtype != SPIRAL_DTYPE_F32)
+    return fail(SPIRAL_ERR_INVALID_ARGUMENT, "y_dtype %d is neither F32 nor BF16", y_dtype);
+  if ((flags & SPIRAL_FLAG_ACCUMULATE) && y_dtype != SPIRAL_DTYPE_F32)
+    return fail(SPIRAL_ERR_INVALID_ARGUMENT, "ACCUMULATE needs an F32 destination");
+  if (w_row_stride_bytes < row_bytes(fmt, K))
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "w row stride %lld < row bytes %lld", (long long)w_row_stride_bytes,
+                (long long)row_bytes(fmt, K));
+  if (x_row_stride_elems < K || y_row_stride_elems < N)
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "x/y row strides smaller than K/N");
+  if ((reinterpret_cast<uintptr_t>(w) & 1u) || (w_row_stride_bytes & 1) || (reinterpret_cast<uintptr_t>(x) & 1u) ||
+      (reinterpret_cast<uintptr_t>(y) & (y_dtype == SPIRAL_DTYPE_F32 ? 3u : 1u)))
+    return fail(SPIRAL_ERR_ALIGNMENT, "w/x/y misaligned for their element types");
+  MatArgs a{};
+  a.fmt = fmt;
+  a.w = static_cast<const uint8_t*>(w);
+  a.w_stride = w_row_stride_bytes;
+  a.x = static_cast<const uint16_t*>(x);
+  a.x_s8 = 8;
+  a.x_sm = x_row_stride_elems;
+  a.y = y;
+  a.y_s8 = 8;
+  a.y_sm = y_row_stride_elems;
+  a.y_bf16 = y_dtype == SPIRAL_DTYPE_BF16;
+  a.accumulate = (flags & SPIRAL_FLAG_ACCUMULATE) != 0;
+  a.ftz = (flags & SPIRAL_FLAG_FTZ_SCALES) != 0;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  return run_mat(a, static_cast<cudaStream_t>(stream));
+}
+
+int spiral_quants_unpack_mmul_all(int fmt, const void* packed, const void* inputs_bf16, float* outputs,
+                                  int64_t weights_rows, int64_t weights_cols, int64_t inputs_vecs, unsigned flags,
+                                  void* stream) {
+  g_last_error[0] = 0;
+  if (int st = check_shape(fmt, weights_rows, weights_cols)) return st;
+  if (weights_cols % 8 != 0 || weights_rows % 8 != 0)
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "weights_rows and weights_cols must be multiples of 8");
+  if (inputs_vecs <= 0) return fail(SPIRAL_ERR_INVALID_SHAPE, "inputs_vecs must be positive");
+  if (packed == nullptr || inputs_bf16 == nullptr || outputs == nullptr)
+    return fail(SPIRAL_ERR_NULL_POINTER, "null packed, inputs or outputs");
+  if ((reinterpret_cast<uintptr_t>(packed) & 1u) || (reinterpret_cast<uintptr_t>(inputs_bf16) & 1u) ||
+      (reinterpret_cast<uintptr_t>(outputs) & 3u))
+    return fail(SPIRAL_ERR_ALIGNMENT, "packed/inputs/outputs misaligned");
+  MatArgs a{};
+  a.fmt = fmt;
+  a.w = static_cast<const uint8_t*>(packed);
+  a.w_stride = row_bytes(fmt, weights_rows);
+  a.x = static_cast<const uint16_t*>(inputs_bf16);
+  a.x_s8 = 8 * inputs_vecs;
+  a.x_sm = 8;
+  a.y = outputs;
+  a.y_s8 = 8 * inputs_vecs;
+  a.y_sm = 8;
+  a.y_bf16 = false;
+  a.accumulate = true;
+  a.ftz = (flags & SPIRAL_FLAG_FTZ_SCALES) != 0;
+  a.M = inputs_vecs;
+  a.N = weights_cols;
+  a.K = weights_rows;
+  return run_mat(a, static_cast<cudaStream_t>(stream));
+}
+
+int spiral_device_status(void* stream, uint32_t* code) {
+  g_last_error[0] = 0;
+  if (code == nullptr) return fail(SPIRAL_ERR_NULL_POINTER, "null code");
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "stream sync");
+  uint32_t v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "read device error word");
+  *code = v;
+  if (v != 0) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_fail(e, "clear device error word");
+    return fail(SPIRAL_ERR_TIMEOUT, "device reported error bits 0x%x", v);
+  }
+  return SPIRAL_OK;
+}
+
+}  // extern "C"

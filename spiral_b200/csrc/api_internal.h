@@ -1,0 +1,47 @@
+// api_internal.h — launcher declarations shared between the kernel files and
+// the C-ABI layer (api.cu).  Launchers validate nothing: api.cu checks every
+// argument before calling them.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+namespace spiral {
+
+// dequant.cu
+bool dequant_fast_ok(int fmt, const void* src, int64_t src_stride, const void* dst, int64_t dst_stride, int64_t K);
+cudaError_t dequant_rows(int fmt, const void* src, int64_t src_stride, void* dst, int64_t dst_stride, int64_t K,
+                         int64_t N, bool ftz, cudaStream_t stream);
+cudaError_t dequant_tiles_ref(int fmt, const void* src, int64_t src_stride, void* dst, int64_t K, int64_t N, bool ftz,
+                              cudaStream_t stream);
+
+// Generalised strided operands shared by the GEMV and GEMM paths:
+//   x[m][k] at x + (k/8)*x_s8 + m*x_sm + (k%8)     (bf16 elements)
+//   y[m][n] at y + (n/8)*y_s8 + m*y_sm + (n%8)     (y_dtype elements)
+// Row-major operands use s8 = 8 and sm = row stride; the reference's tiled
+// orders ([K/8][M][8], [N/8][M][8]) use s8 = 8*M and sm = 8.
+struct MatArgs {
+  int fmt;
+  const uint8_t* w;
+  int64_t w_stride;  // bytes between output-feature rows
+  const uint16_t* x;
+  int64_t x_s8, x_sm;
+  void* y;
+  int64_t y_s8, y_sm;
+  bool y_bf16;
+  bool accumulate;
+  bool ftz;
+  int64_t M, N, K;
+};
+
+// gemv.cu — M <= 8.
+bool gemv_fast_ok(const MatArgs& a);
+cudaError_t gemv(const MatArgs& a, cudaStream_t stream);
+
+// Device properties cached per device.
+int device_sm_count();
+size_t device_max_smem_optin();
+
+}  // namespace spiral

@@ -1,0 +1,161 @@
+// common.cuh — shared device helpers for the sm_100a quantized-weight kernels.
+//
+// Canonical GGUF block layouts (little-endian), as the reference pins them:
+//   Q4_0: [fp16 d][16 B qs]; weight j<16 = qs[j]&15, j>=16 = qs[j-16]>>4,
+//         value (q-8)*d                  (src/quants/q4_0/layout.h:10-16,
+//                                          tests/formats/q4_0.py:47-60)
+//   Q8_0: [fp16 d][32 x int8]; value q*d (q8_0/layout.h:10-13,
+//                                          tests/formats/q8_0.py:43-60)
+//   Q6_K: [ql 128][qh 64][int8 sc 16][fp16 d], 256 weights; for half h and
+//         l < 32: y[128h+32s+l] = d*sc[8h+2s+l/16]*(q6-32) with q6 from
+//         ql[64h+32(s&1)+l] (low nibble for s<2, high for s>=2) and two bits
+//         (qh[32h+l] >> 2s) & 3 on top (q6_k/layout.h:10-15,
+//                                          tests/formats/q6_k.py:55-97)
+// Every product d*int (and d*sc*int) is exact in fp32 (at most 24 significant
+// bits), so "fp32 multiply, one bf16 RNE rounding" reproduces the reference
+// oracle's float32 product .astype(bfloat16) bit for bit.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace spiral {
+
+enum : int { kQ4_0 = 2, kQ8_0 = 8, kQ6_K = 14 };
+
+template <int FMT> struct Fmt;
+template <> struct Fmt<kQ4_0> { static constexpr int kBlockK = 32;  static constexpr int kBlockBytes = 18; };
+template <> struct Fmt<kQ8_0> { static constexpr int kBlockK = 32;  static constexpr int kBlockBytes = 34; };
+template <> struct Fmt<kQ6_K> { static constexpr int kBlockK = 256; static constexpr int kBlockBytes = 210; };
+
+// Device-wide sticky error word.  Bounded waits that give up OR a code in here
+// instead of trapping; the host reads and clears it (spiral_device_status).
+enum : uint32_t {
+  kDevErrMbarTimeout = 1u << 0,
+  kDevErrTmemAlloc = 1u << 1,
+  kDevErrBadLaunch = 1u << 2,
+};
+extern __device__ uint32_t g_device_error;
+
+__device__ __forceinline__ void raise_device_error(uint32_t code) {
+  atomicOr(&g_device_error, code);
+}
+
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+// ----------------------------------------------------------- numerics -----
+
+// fp16 bits -> fp32, exact (subnormals kept).  With ftz, subnormal inputs
+// (exponent 0, mantissa != 0) become +0, as the reference repack stores them
+// for its device path (src/quants/common/repack.h:29-34); zeros keep their
+// sign.
+__device__ __forceinline__ float fp16_bits_to_f32(uint32_t h, bool ftz) {
+  if (ftz && (h & 0x7c00u) == 0u && (h & 0x03ffu) != 0u) return 0.0f;
+  float f;
+  asm("{ .reg .f16 t; mov.b16 t, %1; cvt.f32.f16 %0, t; }" : "=f"(f) : "h"((unsigned short)h));
+  return f;
+}
+
+// Two fp32 -> packed bf16x2 (lo in bits 0-15), round-to-nearest-even.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Unsigned byte i of w placed in an fp32 whose value is 2^23 + byte.
+template <int I>
+__device__ __forceinline__ float byte_as_f32_magic(uint32_t w) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | I));
+}
+
+// --------------------------------------------------------- shared memory --
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 4 bytes at a 2-byte aligned shared address.
+__device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t* p) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const uint32_t sh = static_cast<uint32_t>(a & 3u) * 8u;
+  return __funnelshift_r(w[0], w[1], sh);
+}
+__device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) {
+  return *reinterpret_cast<const uint16_t*>(p);
+}
+
+// --------------------------------------------------- mbarrier + bulk copy --
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on an mbarrier phase: gives up after kWaitLimitNs of device
+// time, records kDevErrMbarTimeout in the device error word and returns
+// false, so callers drain and exit instead of hanging the GPU.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      if (mbar_try_wait(bar, parity)) return true;
+    }
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_device_error(kDevErrMbarTimeout);
+      return false;
+    }
+  }
+}
+
+// L2 policy for data read exactly once (weights streamed by a GEMV).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// 1-D bulk (TMA) copy global -> shared, completion counted on `bar` in bytes.
+// dst, src 16-byte aligned; bytes a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+}  // namespace spiral

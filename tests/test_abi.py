@@ -1,0 +1,140 @@
+"""The C-ABI library loads, exports every declared symbol, and validates its
+arguments on the host (no GPU work is launched by these tests).
+
+The reference's contract for invalid input is "return 0" for the size queries
+and the repack (src/quants/q4_0/repack.h:10-41, TODO.md:331-334); the compute
+entry points return negative spiral_status codes.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+import spiral_b200 as sp
+
+from .conftest import REPO
+
+HEADER = REPO / "include" / "spiral_b200.h"
+
+
+def declared_symbols() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"^SPIRAL_API\s+[\w\s\*]+?\b(spiral_\w+)\s*\(", text, flags=re.M))
+
+
+def test_library_exports_every_declared_symbol():
+    syms = declared_symbols()
+    assert len(syms) >= 12
+    out = subprocess.run(["nm", "-D", "--defined-only", str(sp.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r"\bT (spiral_\w+)", out))
+    assert syms <= exported, syms - exported
+    # the Python mirror binds exactly the declared surface
+    assert set(sp._SIGNATURES) == syms
+    L = sp.lib()
+    for name in syms:
+        assert getattr(L, name) is not None
+
+
+def test_library_has_no_torch_or_oracle_dependency():
+    out = subprocess.run(["ldd", str(sp.LIB_PATH)], capture_output=True, text=True).stdout
+    assert "torch" not in out and "oracle" not in out and "python" not in out
+
+
+def test_version_and_status_strings():
+    L = sp.lib()
+    assert L.spiral_version() >= 100
+    assert L.spiral_status_string(0) == b"ok"
+    assert L.spiral_status_string(-2) == b"invalid shape"
+    assert L.spiral_status_string(12345) == b"unknown status"
+
+
+@pytest.mark.parametrize("fmt,bk,bb", [(sp.Q4_0, 32, 18), (sp.Q8_0, 32, 34), (sp.Q6_K, 256, 210)])
+def test_size_queries(fmt, bk, bb):
+    L = sp.lib()
+    assert L.spiral_quants_block_rows(fmt) == bk
+    assert L.spiral_quants_block_bytes(fmt) == bb
+    assert sp.record_count(fmt, 4096, 14336) == (4096 // bk) * 14336
+    assert sp.packed_bytes(fmt, 4096, 14336) == (4096 // bk) * 14336 * bb
+    # invalid shapes return 0 (reference contract)
+    assert sp.record_count(fmt, bk + 1, 8) == 0
+    assert sp.record_count(fmt, 0, 8) == 0
+    assert sp.record_count(fmt, bk, 0) == 0
+    assert sp.packed_bytes(fmt, -bk, 8) == 0
+    assert sp.packed_bytes(99, 256, 8) == 0
+    assert L.spiral_quants_block_rows(99) == 0
+
+
+def _ref_shim(name):
+    path = REPO / "oracle" / "_ref" / f"quants_host_{name}.so"
+    if not path.exists():
+        pytest.skip("reference host shim not built (make -C oracle ref)")
+    L = ctypes.CDLL(str(path))
+    L.quants_packed_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
+    L.quants_packed_bytes.restype = ctypes.c_int64
+    return L
+
+
+@pytest.mark.parametrize("name", ["q4_0", "q8_0", "q6_k"])
+def test_packed_bytes_agree_with_reference_shim(name):
+    """For the reference's own shape rules (rows % 256, cols % 8) the
+    reference's repacked size equals the canonical size this library reads,
+    so buffers sized with either query are interchangeable."""
+    ref = _ref_shim(name)
+    for rows, cols in ((256, 64), (4096, 4096), (4096, 14336), (768, 2048)):
+        assert sp.packed_bytes(name, rows, cols) == ref.quants_packed_bytes(rows, cols)
+    assert ref.quants_packed_bytes(100, 8) == 0 and sp.packed_bytes(name, 100, 8) == 0
+
+
+def test_repack_rejects_invalid_input_with_zero():
+    # no device memory is touched: every case fails validation first
+    assert sp.repack(sp.Q4_0, 0, 2304, 0, 1 << 20, 4096, 8) == 0  # null pointers
+    assert sp.repack(sp.Q4_0, 16, 2303, 32, 1 << 20, 4096, 8) == 0  # stride < row
+    assert sp.repack(sp.Q4_0, 16, 2304, 32, 100, 4096, 8) == 0  # capacity
+    assert sp.repack(sp.Q4_0, 16, 2304, 32, 1 << 20, 4097, 8) == 0  # shape
+
+
+def _call_mul_mat(**kw):
+    a = dict(fmt=sp.Q4_0, w=16, ws=2304, x=16, xs=4096, y=16, yd=sp.BF16, ys=8, M=1, N=8, K=4096, flags=0)
+    a.update(kw)
+    return sp.lib().spiral_mul_mat(a["fmt"], a["w"], a["ws"], a["x"], a["xs"], a["y"], a["yd"], a["ys"], a["M"],
+                                   a["N"], a["K"], a["flags"], 0)
+
+
+def test_mul_mat_validation_codes():
+    assert _call_mul_mat(fmt=3) == -1
+    assert _call_mul_mat(K=4001) == -2 and b"K=4001" in sp.lib().spiral_last_error()
+    assert _call_mul_mat(K=4001) == -2
+    assert _call_mul_mat(M=0) == -2
+    assert _call_mul_mat(N=-1) == -2
+    assert _call_mul_mat(w=0) == -3
+    assert _call_mul_mat(x=0) == -3
+    assert _call_mul_mat(yd=7) == -10
+    assert _call_mul_mat(flags=sp.FLAG_ACCUMULATE) == -10  # accumulate needs f32
+    assert _call_mul_mat(ws=100) == -2
+    assert _call_mul_mat(xs=10) == -2
+    assert _call_mul_mat(w=17) == -4
+
+
+def test_dequant_and_unpack_validation_codes():
+    L = sp.lib()
+    assert L.spiral_dequant_bf16(sp.Q6_K, 16, 3360, 16, 4096, 4000, 8, 0, 0) == -2
+    assert L.spiral_dequant_bf16(sp.Q6_K, 0, 3360, 16, 4096, 4096, 8, 0, 0) == -3
+    assert L.spiral_dequant_bf16(sp.Q6_K, 16, 3000, 16, 4096, 4096, 8, 0, 0) == -2
+    assert L.spiral_dequant_bf16(sp.Q6_K, 17, 3360, 16, 4096, 4096, 8, 0, 0) == -4
+    assert L.spiral_quants_unpack_all(sp.Q8_0, 16, 16, 256, 60, 0, 0) == -2  # cols % 8
+    assert L.spiral_quants_unpack_all(sp.Q8_0, 16, 18, 256, 64, 0, 0) == -4  # 16B output
+    assert L.spiral_quants_unpack_mmul_all(sp.Q8_0, 16, 16, 16, 256, 64, 0, 0, 0) == -2
+    assert L.spiral_quants_unpack_mmul_all(sp.Q8_0, 0, 16, 16, 256, 64, 4, 0, 0) == -3
+    assert L.spiral_quants_unpack_mmul_all(sp.Q8_0, 16, 16, 18, 256, 64, 4, 0, 0) == -4
+
+
+def test_python_mirror_raises_on_error():
+    with pytest.raises(sp.SpiralError) as e:
+        sp._check(sp.lib().spiral_dequant_bf16(sp.Q4_0, 0, 18, 16, 32, 32, 1, 0, 0))
+    assert e.value.status == -3

@@ -1,0 +1,129 @@
+"""Fused dequant-GEMV (decode, M <= 8) on the GPU against the oracle.
+
+Two levels, as in the reference (src/quants/NOTES.md:540-553):
+* the reference's own fused-mmul cases (mmul.py, tiled I/O, accumulate into
+  caller-zeroed fp32 outputs), checked with the reference's criterion
+  allclose(rtol=1e-3, atol=1e-3) and a tighter bound;
+* BASELINE config 2 shapes (14336 x 4096, B = 1..8) for all three formats,
+  against the float64 dequant-then-matmul oracle with the stated tolerance
+  (tests/gpu_util.tolerance_ok).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+import spiral_b200 as sp
+from oracle import formats as F
+
+from .conftest import load_golden
+from .gpu_util import dev_bf16, dev_bytes, host_bits, tolerance_ok
+
+pytestmark = pytest.mark.gpu
+FMTS = [F.Q4_0, F.Q8_0, F.Q6_K]
+
+
+@pytest.mark.parametrize("fid", FMTS, ids=lambda f: F.NAMES[f])
+@pytest.mark.parametrize("seed", [1, 2, 3])
+def test_unpack_mmul_all_reference_cases(cuda, fid, seed):
+    import torch
+
+    g = load_golden(f"ref_default_{F.NAMES[fid]}_s{seed}.npz")
+    K, N = int(g["K"]), int(g["N"])
+    outputs = torch.zeros(N * 4, dtype=torch.float32, device="cuda")
+    sp.unpack_mmul_all(fid, dev_bytes(g["raw"]), dev_bf16(g["inputs_tiled"]), outputs, K, N, 4)
+    got = outputs.cpu().numpy().reshape(N // 8, 4, 8).transpose(1, 0, 2).reshape(4, N)
+    want = g["expected_outputs"]
+    assert np.allclose(got, want, rtol=1e-3, atol=1e-3)  # the reference's own check
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5 * np.abs(want).max())
+    # accumulate semantics: a second call adds the same product again
+    sp.unpack_mmul_all(fid, dev_bytes(g["raw"]), dev_bf16(g["inputs_tiled"]), outputs, K, N, 4)
+    got2 = outputs.cpu().numpy().reshape(N // 8, 4, 8).transpose(1, 0, 2).reshape(4, N)
+    np.testing.assert_allclose(got2, 2 * want, rtol=1e-5, atol=2e-5 * np.abs(want).max())
+
+
+@pytest.fixture(scope="module")
+def big_weights():
+    cache = {}
+
+    def get(fid, K, N, seed=0):
+        key = (fid, K, N, seed)
+        if key not in cache:
+            cache[key] = F.generate(fid, K, N, seed)
+        return cache[key]
+
+    return get
+
+
+@pytest.mark.parametrize("fid", FMTS, ids=lambda f: F.NAMES[f])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 8])
+def test_gemv_baseline_config2(cuda, big_weights, fid, M):
+    K, N = 4096, 14336
+    raw = big_weights(fid, K, N)
+    x = F.gen_activations(M, K, seed=100 + M)
+    ref = oracle.mul_mat_f64(fid, raw, x, K, N)
+    w = dev_bytes(raw)
+    xd = dev_bf16(x)
+    y32 = sp.mul_mat(fid, w, xd, N, K, y_dtype=sp.F32).cpu().numpy()
+    ok, rel = tolerance_ok(y32, ref, bf16_out=False)
+    assert ok, rel
+    assert rel < 1e-5, rel  # fp32 accumulate: only summation order differs
+    y16 = host_bits(sp.mul_mat(fid, w, xd, N, K, y_dtype=sp.BF16))
+    ok, rel = tolerance_ok(F.bf16_bits_to_f32(y16), ref, bf16_out=True)
+    assert ok, rel
+
+
+@pytest.mark.parametrize("fid", FMTS, ids=lambda f: F.NAMES[f])
+@pytest.mark.parametrize(
+    "M,N,K",
+    [
+        (1, 1, 2048),  # one output feature
+        (5, 37, 4096),  # ragged N (partial 16-row tile)
+        (8, 4096, 4096),
+        (2, 2048, 768),  # MoE down-projection K (partial chunk)
+        (3, 96, 1536),  # Gemma K: Q6_K generic path
+        (12, 64, 2048),  # M > 8: batched GEMV launches
+    ],
+)
+def test_gemv_shapes(cuda, fid, M, N, K):
+    if K % F.BLOCK_K[fid]:
+        pytest.skip("K not a block multiple")
+    raw = F.generate(fid, K, N, seed=N + K)
+    x = F.gen_activations(M, K, seed=M * 7)
+    ref = oracle.mul_mat_f64(fid, raw, x, K, N)
+    y = sp.mul_mat(fid, dev_bytes(raw), dev_bf16(x), N, K, y_dtype=sp.F32).cpu().numpy()
+    ok, rel = tolerance_ok(y, ref, bf16_out=False)
+    assert ok, rel
+
+
+@pytest.mark.parametrize("fid", FMTS, ids=lambda f: F.NAMES[f])
+def test_gemv_strides_accumulate_ftz(cuda, fid):
+    import torch
+
+    K, N, M = 4096, 300, 4
+    raw = F.generate(fid, K, N, seed=11)
+    x = F.gen_activations(M, K, seed=12)
+    # strided activations and outputs inside larger buffers
+    xbig = np.zeros((M, K + 64), dtype=np.uint16)
+    xbig[:, :K] = x
+    y = torch.full((M, N + 8), 0.5, dtype=torch.float32, device="cuda")
+    sp.mul_mat(fid, dev_bytes(raw), dev_bf16(xbig), N, K, y, y_dtype=sp.F32, x_row_stride=K + 64,
+               y_row_stride=N + 8, accumulate=True, ftz=True)
+    ref = oracle.mul_mat_f64(fid, raw, x, K, N, ftz=True) + 0.5
+    got = y.cpu().numpy()
+    ok, rel = tolerance_ok(got[:, :N], ref, bf16_out=False)
+    assert ok, rel
+    assert np.all(got[:, N:] == 0.5)
+
+
+def test_gemv_is_deterministic(cuda, big_weights):
+    K, N = 4096, 14336
+    raw = big_weights(F.Q4_0, K, N)
+    x = dev_bf16(F.gen_activations(8, K, seed=1))
+    w = dev_bytes(raw)
+    a = sp.mul_mat(F.Q4_0, w, x, N, K, y_dtype=sp.F32).cpu().numpy()
+    b = sp.mul_mat(F.Q4_0, w, x, N, K, y_dtype=sp.F32).cpu().numpy()
+    assert np.array_equal(a, b)
+    assert sp.device_status() == 0
