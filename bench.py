@@ -55,7 +55,39 @@ def parse_args(argv=None):
     ap.add_argument("--fmt", default="q4_0", choices=("q4_0", "q8_0", "q6_k"))
     ap.add_argument("--no-extras", action="store_true", help="skip the per-format / per-batch extras")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--profile", choices=("gemv", "dequant"), default=None,
+                    help="ncu helper: run --warmup + --steps eager launches of one kernel on one GPU "
+                         "(B from --batch), nothing else")
+    ap.add_argument("--batch", type=int, default=1, help="activation vectors for --profile gemv")
     return ap.parse_args(argv)
+
+
+def run_profile(args):
+    """A few plain launches of one kernel for ncu (fresh weight copies per
+    launch so every launch reads HBM)."""
+    import torch
+
+    import spiral_b200 as sp
+    from oracle import formats as F
+
+    torch.cuda.set_device(0)
+    fid = F.BY_NAME[args.fmt]
+    K, N = K_DIM, (N_DIM if args.profile == "gemv" or args.fmt != "q4_0" else 4096)
+    raw = F.generate(fid, K, N, seed=0)
+    n = args.warmup + args.steps
+    ws = [torch.from_numpy(raw).cuda() for _ in range(min(n, 8))]
+    if args.profile == "gemv":
+        x = torch.from_numpy(F.gen_activations(args.batch, K, seed=1).view(np.int16)).cuda().view(torch.bfloat16)
+        y = torch.empty((args.batch, N), dtype=torch.bfloat16, device="cuda")
+        for i in range(n):
+            sp.mul_mat(fid, ws[i % len(ws)], x, N, K, y, y_dtype=sp.BF16)
+    else:
+        out = torch.empty((N, K), dtype=torch.bfloat16, device="cuda")
+        for i in range(n):
+            sp.dequant_bf16(fid, ws[i % len(ws)], K, N, out)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": args.profile, "fmt": args.fmt, "launches": n, "device_status": sp.device_status()}))
+    return 0
 
 
 def dist_env():
@@ -472,6 +504,8 @@ def bench_extras(sp, F, dev, K, N, timed, graph_steps, hbm_peak):
 
 def main(argv=None):
     args = parse_args(argv)
+    if args.profile:
+        return run_profile(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_spiral(args)

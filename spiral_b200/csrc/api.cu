@@ -195,11 +195,16 @@ int spiral_quants_unpack_all(int fmt, const void* packed, void* weights_bf16, in
 
 namespace {
 
-// Runs y = x W^T for any M by slicing the activation vectors into batches of
-// at most 8 for the GEMV kernel.  (Large M is served by the GEMM kernel once
-// it is selected by spiral_mul_mat.)
+// Runs y = x W^T.  M <= 8: the fused GEMV.  Larger M: the tcgen05 GEMM when
+// the operands allow it (row-major, 16-byte aligned, K % 256 == 0), else the
+// GEMV over batches of at most 8 activation vectors.
 int run_mat(MatArgs a, cudaStream_t stream) {
   const int64_t M = a.M;
+  if (M > 8 && gemm_supported(a)) {
+    const cudaError_t e = gemm(a, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+    return SPIRAL_OK;
+  }
   for (int64_t m0 = 0; m0 < M; m0 += 8) {
     MatArgs b = a;
     b.M = std::min<int64_t>(8, M - m0);

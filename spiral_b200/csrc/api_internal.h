@@ -40,6 +40,10 @@ struct MatArgs {
 bool gemv_fast_ok(const MatArgs& a);
 cudaError_t gemv(const MatArgs& a, cudaStream_t stream);
 
+// gemm.cu — tcgen05 dequant-GEMM for larger M.
+bool gemm_supported(const MatArgs& a);
+cudaError_t gemm(const MatArgs& a, cudaStream_t stream);
+
 // Device properties cached per device.
 int device_sm_count();
 size_t device_max_smem_optin();

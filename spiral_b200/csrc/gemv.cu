@@ -3,34 +3,37 @@
 // B200 counterpart of the reference's fused unpack_mmul
 // (src/quants/q4_0/mmul.aie.h:16-90, q8_0/mmul.aie.h:16-117,
 // q6_k/mmul.aie.h:18-84): out[m][n] = sum_k in[m][k] * bf16(W[n][k]) with
-// fp32 accumulation.  The weights are streamed from HBM exactly once.
+// fp32 accumulation.  Weights stream from HBM exactly once.
 //
-// Structure (one persistent CTA per SM, 8 consumer warps + 1 producer warp):
-//  * A "tile" is 16 output features (one m16 MMA row block) over all of K.
-//    Tiles are dealt to CTAs round-robin.
-//  * The producer lane streams each tile's rows chunk by chunk (up to 8
-//    "groups" of K per chunk) with 1-D bulk (TMA) copies into a ring of shared
-//    stages, one copy per row, completion counted in bytes on an mbarrier.
-//    Weights use an L2 evict-first policy: they are read once.
-//  * Consumer warp w takes group w of every chunk (a K-split inside the CTA),
-//    dequantizes it in registers straight into the bf16 A fragments of
-//    mma.sync.m16n8k16 (rows = features, k = 16 weights, n = 8 activation
-//    vectors, padded), and accumulates in fp32.  At the end of a tile the 8
-//    warps' partial 16x8 tiles are summed in a fixed order (deterministic)
-//    and stored.
-//  * Activations x are staged once per CTA into shared memory in a k order
-//    permuted to match how each lane's A fragment is decoded, so every B
-//    fragment is one conflict-free 8-byte shared load.  The MMA contracts
-//    over k, so permuting k identically in A and B leaves the sum unchanged.
+// Structure (one persistent CTA per SM; two consumer groups of 8 warps plus
+// one producer warp):
+//  * A tile is 16 output features (one m16 MMA row block).  Tiles are dealt to
+//    CTAs round-robin, and inside a CTA to its consumer groups round-robin, so
+//    two tiles are being decoded while the producer prefetches the next ones.
+//  * A pipeline stage holds the tile's rows over a K chunk (the whole row
+//    whenever it fits, so one stage per tile).  The producer lane fills it
+//    with one 1-D bulk (TMA) copy per row into a padded row pitch, completion
+//    counted in bytes on an mbarrier; weights use an L2 evict-first policy.
+//  * Consumer warp w of a group decodes the K groups w, w+8, ... of the stage
+//    in registers straight into bf16 A fragments of mma.sync.m16n8k16 (rows
+//    = features, n = 8 activation vectors, padded) and accumulates in fp32.
+//    At the end of a tile the group's 8 partial 16x8 tiles are summed in a
+//    fixed order (deterministic) and stored.
+//  * Activations are staged once per CTA in shared memory in a k order
+//    permuted to match each lane's A fragment, so a B fragment is one 8-byte
+//    shared load.  The MMA contracts over k, so permuting k identically in A
+//    and B leaves the sum unchanged.
 //
-// Exactness: the A fragments are the same bf16 weights the standalone
-// dequant produces (bf16_rne(d*int)), so results differ from the reference's
-// dequant-then-fp32-matmul only by fp32 summation order.  Q4_0 uses a packed
-// bf16 form of the exact product: d = hi + lo with hi = bf16(d) and lo =
-// bf16(d - hi) exact (fp16 d has 11 significant bits), t = q - 8 exact, and
-// fma.rn.bf16x2(t, hi, t*lo) = bf16_rne(t*hi + t*lo) = bf16_rne(t*d) since
-// t*lo is exact in bf16.  (The only difference from the fp32 route is the
-// sign of a zero weight, which cannot change a dot product.)
+// Dequantization (exact): a quant byte is placed in the mantissa of an fp32
+// with one byte permute, f = 1 + q*2^-s, and one fused multiply-add computes
+// f*(2^s*d) - (2^s + bias)*d = (q - bias)*d.  Both constants are exact in
+// fp32 (at most 24 significant bits) and so is the result, so the FMA does
+// not round; cvt.rn.bf16x2.f32 then rounds once to nearest even.  The A
+// fragments therefore hold exactly the bf16 weights of the standalone
+// dequant (bf16_rne(d*int), up to the sign of a zero weight, which cannot
+// change a dot product), and the GEMV differs from the reference's
+// dequant-then-fp32-matmul only by fp32 summation order.  Pairs of weights
+// go through one fma.rn.f32x2.
 #include <atomic>
 
 #include "api_internal.h"
@@ -39,25 +42,25 @@
 namespace spiral {
 
 template <int FMT> struct GemvFmt;
-// kGroupK weights per group; one group is what a consumer warp decodes per
-// chunk.  kSteps = kGroupK / 16 MMA k-steps.  A chunk holds up to 8 groups of
-// every tile row and is always a 16-byte multiple (2 groups for Q4_0/Q8_0, 8
-// super-blocks for Q6_K).
+// kGroupK weights per group (the unit a consumer warp decodes); kSteps MMA
+// k-steps per group; a chunk must be a multiple of kChunkAlign groups to stay
+// 16-byte aligned.
 template <> struct GemvFmt<kQ4_0> {
-  static constexpr int kGroupK = 128, kGroupBytes = 72, kSteps = 8, kStages = 8, kGroupAlign = 2;
+  static constexpr int kGroupK = 128, kGroupBytes = 72, kSteps = 8, kChunkAlign = 2, kMaxStages = 4;
 };
 template <> struct GemvFmt<kQ8_0> {
-  static constexpr int kGroupK = 128, kGroupBytes = 136, kSteps = 8, kStages = 5, kGroupAlign = 2;
+  static constexpr int kGroupK = 128, kGroupBytes = 136, kSteps = 8, kChunkAlign = 2, kMaxStages = 4;
 };
 template <> struct GemvFmt<kQ6_K> {
-  static constexpr int kGroupK = 256, kGroupBytes = 210, kSteps = 16, kStages = 4, kGroupAlign = 8;
+  static constexpr int kGroupK = 256, kGroupBytes = 210, kSteps = 16, kChunkAlign = 8, kMaxStages = 4;
 };
 
-constexpr int kConsumerWarps = 8;
-constexpr int kChunkGroups = kConsumerWarps;
+constexpr int kGroupsPerCta = 2;  // consumer groups
+constexpr int kWarpsPerGroup = 8;
+constexpr int kConsumerWarps = kGroupsPerCta * kWarpsPerGroup;
 constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
 constexpr int kTileRows = 16;
-constexpr int kBarrierBytes = 256;  // room for up to 16 mbarriers
+constexpr int kBarrierBytes = 256;  // up to 15 mbarrier pairs + the abort word
 constexpr int kRedBytes = kConsumerWarps * 32 * 16;
 
 struct GemvParams {
@@ -70,11 +73,12 @@ struct GemvParams {
   int64_t N, K;
   int64_t groups_per_row;
   int M;
+  int chunk_groups;  // groups per full chunk
   int chunks_per_row;
   int stages;
   int row_pitch;  // bytes per row slot in a stage
   int x_pitch;    // bytes per activation vector in the permuted copy
-  int y_bf16, accumulate, ftz, x_vec16;
+  int y_bf16, accumulate, ftz, x_vec8;
 };
 
 // ------------------------------------------------------------- helpers ---
@@ -88,195 +92,216 @@ __device__ __forceinline__ void mma_bf16_16816(float (&acc)[4], uint32_t a0, uin
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// Two fp32 bit patterns through one exact fma.rn.f32x2 with (D, C), then one
+// RNE pack to bf16x2 (fa in the low half).
+__device__ __forceinline__ uint32_t fma2_pack(uint32_t fa, uint32_t fb, uint64_t D2, uint64_t C2) {
+  const uint64_t in = (static_cast<uint64_t>(fb) << 32) | fa;
+  uint64_t out;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(out) : "l"(in), "l"(D2), "l"(C2));
+  return pack_bf16x2(__uint_as_float(static_cast<uint32_t>(out)), __uint_as_float(static_cast<uint32_t>(out >> 32)));
 }
-__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-__device__ __forceinline__ uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t r;
-  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
-  return r;
+__device__ __forceinline__ uint64_t dup2(float v) {
+  const uint64_t b = __float_as_uint(v);
+  return (b << 32) | b;
 }
 
-// Exact split of an fp32 value with <= 16 significant bits into bf16 hi + lo,
-// each broadcast into both halves of a bf16x2 word.
-__device__ __forceinline__ void split_scale_bf16x2(float d, uint32_t& hi2, uint32_t& lo2) {
-  const uint32_t hi = pack_bf16x2(d, d);
-  const float hf = __uint_as_float(hi << 16);
-  const float lf = d - hf;  // exact
-  lo2 = pack_bf16x2(lf, lf);
-  hi2 = hi;
+// Byte i of w into bits 8..15 of 0x3F80_00_00: f = 1 + byte * 2^-15.
+template <int I>
+__device__ __forceinline__ uint32_t byte_to_f1(uint32_t w) {
+  return __byte_perm(w, 0x3F800000u, 0x7604u | (I << 4));
 }
-
-// Two Q4_0 weights from nibbles at bits [0,4) and [16,20) of w.
-__device__ __forceinline__ uint32_t q4_0_pair(uint32_t w, uint32_t hi2, uint32_t lo2) {
-  const uint32_t v = (w & 0x000F000Fu) | 0x43004300u;  // bf16 128 + q
-  const uint32_t t = bf16x2_sub(v, 0x43084308u);       // q - 8, exact
-  return bf16x2_fma(t, hi2, bf16x2_mul(t, lo2));
+// Byte i of w (its bit 7 set) into bits 16..23 of 0x3F_00_00_00:
+// f = 1 + (byte & 0x7f) * 2^-7.
+template <int I>
+__device__ __forceinline__ uint32_t byte_to_f2(uint32_t w) {
+  return __byte_perm(w, 0x3F000000u, 0x7054u | (I << 8));
 }
 
 // --------------------------------------------- per-format group decoders --
 // ra / rb: this lane's two feature rows (r and r + 8) at the group start in
-// the stage; c = lane % 4; xg = this lane's B-fragment column at step 0 of
-// the group in the permuted activations (stride 32 bytes per step).
+// the stage (4-byte aligned for Q4_0/Q8_0, 2-byte for Q6_K); c = lane % 4;
+// xg = this lane's B-fragment column at step 0 of the group in the permuted
+// activations (stride 32 bytes per step).  xk(s, c) gives the k offset
+// (within the group) of the 4 consecutive weights lane column c contracts at
+// step s; the activation staging uses it to build the permuted copy.
 
 template <int FMT>
-__device__ __forceinline__ void group_mma(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg, bool ftz,
-                                          float (&acc)[4]);
+struct GroupDecoder;
 
-// Q4_0: lane c owns block c of the 4-block group.  Step s uses qs word
-// j = s/2: pairs (weights 4j+o, 4j+o+2) and (16+4j+o, 16+4j+o+2), o = s%2.
+// Q4_0: lane c owns block c of the 4-block group (18 bytes at 18c).  Step
+// 2j covers the low nibbles of qs word j (weights 4j..4j+3), step 2j+1 the
+// high nibbles (weights 16+4j..16+4j+3).
 template <>
-__device__ __forceinline__ void group_mma<kQ4_0>(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg,
-                                                 bool ftz, float (&acc)[4]) {
-  const uint8_t* ba = ra + 18 * c;
-  const uint8_t* bb = rb + 18 * c;
-  uint32_t hia, loa, hib, lob;
-  split_scale_bf16x2(fp16_bits_to_f32(lds_u16(ba), ftz), hia, loa);
-  split_scale_bf16x2(fp16_bits_to_f32(lds_u16(bb), ftz), hib, lob);
-  uint32_t qa[4], qb[4];
+struct GroupDecoder<kQ4_0> {
+  __device__ __forceinline__ static void run(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg, bool ftz,
+                                             float (&acc)[4]) {
+    // qs starts at 18c + 2: 4-byte aligned for odd c, 2 mod 4 for even c.
+    const int woff = 18 * c + 2 * (c & 1);
+    const uint32_t sh = (c & 1) ? 0u : 16u;
+    uint32_t qa[4], qb[4];
+    {
+      uint32_t wa[5], wb[5];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    qa[j] = lds_u32_a2(ba + 2 + 4 * j);
-    qb[j] = lds_u32_a2(bb + 2 + 4 * j);
-  }
+      for (int i = 0; i < 5; ++i) {
+        wa[i] = lds32(ra + woff + 4 * i);
+        wb[i] = lds32(rb + woff + 4 * i);
+      }
 #pragma unroll
-  for (int s = 0; s < 8; ++s) {
-    const int j = s >> 1;
-    const uint32_t wa = (s & 1) ? (qa[j] >> 8) : qa[j];
-    const uint32_t wb = (s & 1) ? (qb[j] >> 8) : qb[j];
-    const uint2 b = *reinterpret_cast<const uint2*>(xg + 32 * s);
-    mma_bf16_16816(acc, q4_0_pair(wa, hia, loa), q4_0_pair(wb, hib, lob), q4_0_pair(wa >> 4, hia, loa),
-                   q4_0_pair(wb >> 4, hib, lob), b.x, b.y);
+      for (int j = 0; j < 4; ++j) {
+        qa[j] = __funnelshift_r(wa[j], wa[j + 1], sh);
+        qb[j] = __funnelshift_r(wb[j], wb[j + 1], sh);
+      }
+    }
+    const float da = fp16_bits_to_f32(lds_u16(ra + 18 * c), ftz);
+    const float db = fp16_bits_to_f32(lds_u16(rb + 18 * c), ftz);
+    // low nibble: f = 1 + q 2^-15; high nibble (16q in the byte): 1 + q 2^-11.
+    // 2^15 + 8 = 8 * 4097 and 2^11 + 8 = 8 * 257 keep the bias products exact.
+    const uint64_t DLa = dup2(da * 32768.0f), CLa = dup2(da * -32776.0f);
+    const uint64_t DHa = dup2(da * 2048.0f), CHa = dup2(da * -2056.0f);
+    const uint64_t DLb = dup2(db * 32768.0f), CLb = dup2(db * -32776.0f);
+    const uint64_t DHb = dup2(db * 2048.0f), CHb = dup2(db * -2056.0f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t la = qa[j] & 0x0F0F0F0Fu, ha = qa[j] & 0xF0F0F0F0u;
+      const uint32_t lb = qb[j] & 0x0F0F0F0Fu, hb = qb[j] & 0xF0F0F0F0u;
+      const uint2 b0 = *reinterpret_cast<const uint2*>(xg + 32 * (2 * j));
+      mma_bf16_16816(acc, fma2_pack(byte_to_f1<0>(la), byte_to_f1<1>(la), DLa, CLa),
+                     fma2_pack(byte_to_f1<0>(lb), byte_to_f1<1>(lb), DLb, CLb),
+                     fma2_pack(byte_to_f1<2>(la), byte_to_f1<3>(la), DLa, CLa),
+                     fma2_pack(byte_to_f1<2>(lb), byte_to_f1<3>(lb), DLb, CLb), b0.x, b0.y);
+      const uint2 b1 = *reinterpret_cast<const uint2*>(xg + 32 * (2 * j + 1));
+      mma_bf16_16816(acc, fma2_pack(byte_to_f1<0>(ha), byte_to_f1<1>(ha), DHa, CHa),
+                     fma2_pack(byte_to_f1<0>(hb), byte_to_f1<1>(hb), DHb, CHb),
+                     fma2_pack(byte_to_f1<2>(ha), byte_to_f1<3>(ha), DHa, CHa),
+                     fma2_pack(byte_to_f1<2>(hb), byte_to_f1<3>(hb), DHb, CHb), b1.x, b1.y);
+    }
   }
-}
+  __host__ __device__ __forceinline__ static int xk(int s, int c) { return 32 * c + 16 * (s & 1) + 4 * (s >> 1); }
+};
 
-// Q8_0: lane c owns block c of the group; step s = weights 4s..4s+3.
-__device__ __forceinline__ uint32_t q8_0_pair(uint32_t w, int i, float d) {
-  constexpr float kBias = 8388736.0f;  // 2^23 + 128
-  const float f0 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | i)) - kBias;
-  const float f1 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | (i + 1))) - kBias;
-  return pack_bf16x2(f0 * d, f1 * d);
-}
+// Q8_0: lane c owns block c (34 bytes at 34c); step s = weights 4s..4s+3.
+// int8 q is biased to u = q + 128 (x ^ 0x80); f = 1 + u 2^-15 and
+// 2^15 + 128 = 128 * 257 keeps the bias product exact.
 template <>
-__device__ __forceinline__ void group_mma<kQ8_0>(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg,
-                                                 bool ftz, float (&acc)[4]) {
-  const uint8_t* ba = ra + 34 * c;
-  const uint8_t* bb = rb + 34 * c;
-  const float da = fp16_bits_to_f32(lds_u16(ba), ftz);
-  const float db = fp16_bits_to_f32(lds_u16(bb), ftz);
+struct GroupDecoder<kQ8_0> {
+  __device__ __forceinline__ static void run(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg, bool ftz,
+                                             float (&acc)[4]) {
+    const int woff = 34 * c + 2 * (c & 1);
+    const uint32_t sh = (c & 1) ? 0u : 16u;
+    const float da = fp16_bits_to_f32(lds_u16(ra + 34 * c), ftz);
+    const float db = fp16_bits_to_f32(lds_u16(rb + 34 * c), ftz);
+    const uint64_t Da = dup2(da * 32768.0f), Ca = dup2(da * -32896.0f);
+    const uint64_t Db = dup2(db * 32768.0f), Cb = dup2(db * -32896.0f);
+    uint32_t pa = lds32(ra + woff), pb = lds32(rb + woff);
 #pragma unroll
-  for (int s = 0; s < 8; ++s) {
-    const uint32_t wa = lds_u32_a2(ba + 2 + 4 * s) ^ 0x80808080u;
-    const uint32_t wb = lds_u32_a2(bb + 2 + 4 * s) ^ 0x80808080u;
-    const uint2 b = *reinterpret_cast<const uint2*>(xg + 32 * s);
-    mma_bf16_16816(acc, q8_0_pair(wa, 0, da), q8_0_pair(wb, 0, db), q8_0_pair(wa, 2, da), q8_0_pair(wb, 2, db), b.x,
-                   b.y);
+    for (int s = 0; s < 8; ++s) {
+      const uint32_t na = lds32(ra + woff + 4 * (s + 1)), nb = lds32(rb + woff + 4 * (s + 1));
+      const uint32_t qa = __funnelshift_r(pa, na, sh) ^ 0x80808080u;
+      const uint32_t qb = __funnelshift_r(pb, nb, sh) ^ 0x80808080u;
+      pa = na;
+      pb = nb;
+      const uint2 b = *reinterpret_cast<const uint2*>(xg + 32 * s);
+      mma_bf16_16816(acc, fma2_pack(byte_to_f1<0>(qa), byte_to_f1<1>(qa), Da, Ca),
+                     fma2_pack(byte_to_f1<0>(qb), byte_to_f1<1>(qb), Db, Cb),
+                     fma2_pack(byte_to_f1<2>(qa), byte_to_f1<3>(qa), Da, Ca),
+                     fma2_pack(byte_to_f1<2>(qb), byte_to_f1<3>(qb), Db, Cb), b.x, b.y);
+    }
   }
-}
+  __host__ __device__ __forceinline__ static int xk(int s, int c) { return 32 * c + 4 * s; }
+};
 
 // Q6_K: one super-block per group; lane c owns l in [8c, 8c+8) of both
 // halves.  Step t = 8h + 4*half + s covers y = 128h + 32s + 8c + 4*half + 0..3.
+// The 6-bit quant with bit 7 set gives f = 1 + q6 2^-7;
+// f*(128 ds) - 160 ds = (q6 - 32) ds with ds = d*sc (exact, <= 18 bits).
 template <>
-__device__ __forceinline__ void group_mma<kQ6_K>(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg,
-                                                 bool ftz, float (&acc)[4]) {
-  const float da = fp16_bits_to_f32(lds_u16(ra + 208), ftz);
-  const float db = fp16_bits_to_f32(lds_u16(rb + 208), ftz);
+struct GroupDecoder<kQ6_K> {
+  // 8 bytes at p (p % 4 == sh/8 for a 2-byte aligned super-block start).
+  __device__ __forceinline__ static void load8(const uint8_t* p, uint32_t sh, uint32_t& lo, uint32_t& hi) {
+    const uint8_t* a = p - (sh >> 3);
+    const uint32_t w0 = lds32(a), w1 = lds32(a + 4), w2 = lds32(a + 8);
+    lo = __funnelshift_r(w0, w1, sh);
+    hi = __funnelshift_r(w1, w2, sh);
+  }
+  __device__ __forceinline__ static uint32_t assemble(uint32_t ql, uint32_t qh, int s) {
+    const uint32_t lo = (s >= 2 ? (ql >> 4) : ql) & 0x0F0F0F0Fu;
+    const uint32_t hb = (s == 0 ? (qh << 4) : s == 1 ? (qh << 2) : s == 2 ? qh : (qh >> 2)) & 0x30303030u;
+    return lo | hb | 0x80808080u;
+  }
+  __device__ __forceinline__ static void run(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg, bool ftz,
+                                             float (&acc)[4], uint32_t sh) {
+    const float da = fp16_bits_to_f32(lds_u16(ra + 208), ftz);
+    const float db = fp16_bits_to_f32(lds_u16(rb + 208), ftz);
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    float dsa[4], dsb[4];
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      const int si = 192 + 8 * h + 2 * s + (c >> 1);
-      dsa[s] = da * static_cast<float>(static_cast<int8_t>(ra[si]));
-      dsb[s] = db * static_cast<float>(static_cast<int8_t>(rb[si]));
-    }
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int o = 8 * c + 4 * half;
-      const uint32_t qla_a = lds_u32_a2(ra + 64 * h + o), qlb_a = lds_u32_a2(ra + 64 * h + 32 + o);
-      const uint32_t qh_a = lds_u32_a2(ra + 128 + 32 * h + o);
-      const uint32_t qla_b = lds_u32_a2(rb + 64 * h + o), qlb_b = lds_u32_a2(rb + 64 * h + 32 + o);
-      const uint32_t qh_b = lds_u32_a2(rb + 128 + 32 * h + o);
+    for (int h = 0; h < 2; ++h) {
+      uint64_t Da[4], Ca[4], Db[4], Cb[4];
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        const uint2 wa = q6_k_scale4(q6_k_assemble4((s & 1) ? qlb_a : qla_a, qh_a, s), dsa[s]);
-        const uint2 wb = q6_k_scale4(q6_k_assemble4((s & 1) ? qlb_b : qla_b, qh_b, s), dsb[s]);
-        const uint2 b = *reinterpret_cast<const uint2*>(xg + 32 * (8 * h + 4 * half + s));
-        mma_bf16_16816(acc, wa.x, wb.x, wa.y, wb.y, b.x, b.y);
+        const int si = 192 + 8 * h + 2 * s + (c >> 1);
+        const float dsa = da * static_cast<float>(static_cast<int8_t>(ra[si]));
+        const float dsb = db * static_cast<float>(static_cast<int8_t>(rb[si]));
+        Da[s] = dup2(dsa * 128.0f);
+        Ca[s] = dup2(dsa * -160.0f);
+        Db[s] = dup2(dsb * 128.0f);
+        Cb[s] = dup2(dsb * -160.0f);
+      }
+      uint32_t qla[2], qlb[2], qha[2], qla_b[2], qlb_b[2], qh_b[2];
+      load8(ra + 64 * h + 8 * c, sh, qla[0], qla[1]);
+      load8(ra + 64 * h + 32 + 8 * c, sh, qlb[0], qlb[1]);
+      load8(ra + 128 + 32 * h + 8 * c, sh, qha[0], qha[1]);
+      load8(rb + 64 * h + 8 * c, sh, qla_b[0], qla_b[1]);
+      load8(rb + 64 * h + 32 + 8 * c, sh, qlb_b[0], qlb_b[1]);
+      load8(rb + 128 + 32 * h + 8 * c, sh, qh_b[0], qh_b[1]);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const uint32_t qa = assemble((s & 1) ? qlb[half] : qla[half], qha[half], s);
+          const uint32_t qb = assemble((s & 1) ? qlb_b[half] : qla_b[half], qh_b[half], s);
+          const uint2 b = *reinterpret_cast<const uint2*>(xg + 32 * (8 * h + 4 * half + s));
+          mma_bf16_16816(acc, fma2_pack(byte_to_f2<0>(qa), byte_to_f2<1>(qa), Da[s], Ca[s]),
+                         fma2_pack(byte_to_f2<0>(qb), byte_to_f2<1>(qb), Db[s], Cb[s]),
+                         fma2_pack(byte_to_f2<2>(qa), byte_to_f2<3>(qa), Da[s], Ca[s]),
+                         fma2_pack(byte_to_f2<2>(qb), byte_to_f2<3>(qb), Db[s], Cb[s]), b.x, b.y);
+        }
       }
     }
   }
-}
+  __host__ __device__ __forceinline__ static int xk(int t, int c) {
+    const int h = t >> 3, half = (t >> 2) & 1, s = t & 3;
+    return 128 * h + 32 * s + 8 * c + 4 * half;
+  }
+};
 
 // ------------------------------------------------- activation staging ----
 
-__device__ __forceinline__ uint4 load_x8(const GemvParams& p, int m, int64_t k) {
-  const uint16_t* base = p.x + (k >> 3) * p.x_s8 + static_cast<int64_t>(m) * p.x_sm;
-  if (p.x_vec16) return __ldg(reinterpret_cast<const uint4*>(base));
-  uint32_t e[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) e[i] = base[i];
-  return make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16), e[6] | (e[7] << 16));
+__device__ __forceinline__ uint2 load_x4(const GemvParams& p, int m, int64_t k) {
+  const uint16_t* base = p.x + (k >> 3) * p.x_s8 + static_cast<int64_t>(m) * p.x_sm + (k & 7);
+  if (p.x_vec8) return *reinterpret_cast<const uint2*>(base);  // k % 4 == 0
+  return make_uint2(base[0] | (static_cast<uint32_t>(base[1]) << 16),
+                    base[2] | (static_cast<uint32_t>(base[3]) << 16));
 }
 
-// Writes the permuted activations: entry (m, group, step, c) = the 4 bf16
-// that lane column c contracts at that step, at
-//   xs + m*x_pitch + (group*kSteps + step)*32 + c*8.
+// Permuted activations: entry (m, group g, step s, lane column c) holds the
+// 4 consecutive k that lane column c contracts at that step, at
+//   xs + m*x_pitch + (g*kSteps + s)*32 + c*8.
 template <int FMT>
 __device__ void stage_x(const GemvParams& p, uint8_t* xs, int tid, int nthreads) {
   using F = GemvFmt<FMT>;
   const int64_t groups = p.K / F::kGroupK;
-  const int64_t units = static_cast<int64_t>(p.M) * groups * 4;
-  for (int64_t u = tid; u < units; u += nthreads) {
-    const int m = static_cast<int>(u / (groups * 4));
-    const int64_t rem = u - static_cast<int64_t>(m) * groups * 4;
-    const int64_t g = rem >> 2;
+  const int64_t per_m = groups * F::kSteps * 4;
+  const int64_t entries = static_cast<int64_t>(p.M) * per_m;
+  for (int64_t e = tid; e < entries; e += nthreads) {
+    const int m = static_cast<int>(e / per_m);
+    const int64_t rem = e - m * per_m;
     const int c = static_cast<int>(rem & 3);
-    uint8_t* out = xs + static_cast<int64_t>(m) * p.x_pitch + g * F::kSteps * 32 + c * 8;
-    if constexpr (FMT == kQ4_0 || FMT == kQ8_0) {
-      const int64_t k0 = g * 128 + 32 * c;  // this lane column's block
-      uint32_t X[16];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 v = load_x8(p, m, k0 + 8 * i);
-        X[4 * i] = v.x;
-        X[4 * i + 1] = v.y;
-        X[4 * i + 2] = v.z;
-        X[4 * i + 3] = v.w;
-      }
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        uint2 e;
-        if constexpr (FMT == kQ4_0) {
-          const int j = s >> 1;
-          const uint32_t sel = (s & 1) ? 0x7632u : 0x5410u;
-          e.x = __byte_perm(X[2 * j], X[2 * j + 1], sel);
-          e.y = __byte_perm(X[8 + 2 * j], X[9 + 2 * j], sel);
-        } else {
-          e.x = X[2 * s];
-          e.y = X[2 * s + 1];
-        }
-        *reinterpret_cast<uint2*>(out + 32 * s) = e;
-      }
-    } else {
-      const int64_t k0 = g * 256 + 8 * c;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          const uint4 v = load_x8(p, m, k0 + 128 * h + 32 * s);
-          *reinterpret_cast<uint2*>(out + 32 * (8 * h + s)) = make_uint2(v.x, v.y);
-          *reinterpret_cast<uint2*>(out + 32 * (8 * h + 4 + s)) = make_uint2(v.z, v.w);
-        }
-      }
-    }
+    const int64_t gs = rem >> 2;  // g*kSteps + s
+    const int64_t g = gs / F::kSteps;
+    const int s = static_cast<int>(gs - g * F::kSteps);
+    const int64_t k = g * F::kGroupK + GroupDecoder<FMT>::xk(s, c);
+    *reinterpret_cast<uint2*>(xs + static_cast<int64_t>(m) * p.x_pitch + gs * 32 + c * 8) = load_x4(p, m, k);
   }
 }
 
@@ -288,13 +313,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + p.stages;
+  // Set when a bounded wait gave up: later waits are skipped (not retried) so
+  // every warp still reaches every named barrier and the kernel ends.
+  int& abort_flag = *reinterpret_cast<int*>(smem + kBarrierBytes - 8);
   float4* red = reinterpret_cast<float4*>(smem + kBarrierBytes);
   uint8_t* xs = smem + kBarrierBytes + kRedBytes;
   uint8_t* stages = xs + static_cast<int64_t>(p.M) * p.x_pitch;
   const int stage_bytes = kTileRows * p.row_pitch;
-  // Set when a bounded wait gave up: later waits are skipped (not retried) so
-  // every warp still reaches every named barrier and the kernel ends.
-  int& abort_flag = *reinterpret_cast<int*>(smem + kBarrierBytes - 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tiles = (p.N + kTileRows - 1) / kTileRows;
@@ -302,7 +327,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], kWarpsPerGroup);
     }
     abort_flag = 0;
     fence_mbar_init();
@@ -325,8 +350,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
             abort_flag = 1;
             goto drain;
           }
-          const int64_t g0 = static_cast<int64_t>(ch) * kChunkGroups;
-          const int ng = static_cast<int>(::spiral::min64(kChunkGroups, p.groups_per_row - g0));
+          const int64_t g0 = static_cast<int64_t>(ch) * p.chunk_groups;
+          const int ng = static_cast<int>(::spiral::min64(p.chunk_groups, p.groups_per_row - g0));
           const uint32_t bytes = static_cast<uint32_t>(ng * F::kGroupBytes);
           mbar_arrive_expect_tx(&full[s], bytes * rows);
           uint8_t* dst = stages + s * stage_bytes;
@@ -344,14 +369,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
 
   // --------------------------------------------------------- consumers -----
   stage_x<FMT>(p, xs, threadIdx.x, kConsumerWarps * 32);
-  named_bar_sync(1, kConsumerWarps * 32);
+  named_bar_sync(kGroupsPerCta + 1, kConsumerWarps * 32);
 
+  const int grp = warp / kWarpsPerGroup, gw = warp % kWarpsPerGroup;
   const int r = lane >> 2, c = lane & 3;
   const int mx = r < p.M ? r : 0;  // vectors >= M read vector 0; their columns are discarded
   const uint8_t* xcol = xs + static_cast<int64_t>(mx) * p.x_pitch + c * 8;
-  uint32_t it = 0;
-  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+  float4* gred = red + grp * kWarpsPerGroup * 32;
+  int64_t local = 0;  // tile index within this CTA
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+    if (local % kGroupsPerCta != grp) continue;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t it = static_cast<uint32_t>(local * p.chunks_per_row);
     for (int ch = 0; ch < p.chunks_per_row; ++ch, ++it) {
       const int s = static_cast<int>(it % p.stages);
       const uint32_t ph = (it / p.stages) & 1u;
@@ -360,23 +389,33 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         ready = mbar_wait(&full[s], ph);
         if (!ready) abort_flag = 1;
       }
-      const int64_t g0 = static_cast<int64_t>(ch) * kChunkGroups;
-      const int ng = static_cast<int>(::spiral::min64(kChunkGroups, p.groups_per_row - g0));
-      if (ready && warp < ng) {
-        const uint8_t* st = stages + s * stage_bytes + warp * F::kGroupBytes;
-        group_mma<FMT>(st + r * p.row_pitch, st + (r + 8) * p.row_pitch, c,
-                       xcol + (g0 + warp) * F::kSteps * 32, p.ftz != 0, acc);
+      const int64_t g0 = static_cast<int64_t>(ch) * p.chunk_groups;
+      const int ng = static_cast<int>(::spiral::min64(p.chunk_groups, p.groups_per_row - g0));
+      if (ready) {
+        const uint8_t* st = stages + s * stage_bytes;
+        const uint8_t* ra = st + r * p.row_pitch;
+        const uint8_t* rb = st + (r + 8) * p.row_pitch;
+        for (int gl = gw; gl < ng; gl += kWarpsPerGroup) {
+          const uint8_t* xg = xcol + (g0 + gl) * F::kSteps * 32;
+          if constexpr (FMT == kQ6_K) {
+            GroupDecoder<FMT>::run(ra + gl * F::kGroupBytes, rb + gl * F::kGroupBytes, c, xg, p.ftz != 0, acc,
+                                   (gl & 1) ? 16u : 0u);
+          } else {
+            GroupDecoder<FMT>::run(ra + gl * F::kGroupBytes, rb + gl * F::kGroupBytes, c, xg, p.ftz != 0, acc);
+          }
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
-    red[warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    named_bar_sync(1, kConsumerWarps * 32);
-    if (threadIdx.x < 128) {
-      const int l = threadIdx.x >> 2, j = threadIdx.x & 3;
+    gred[gw * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    named_bar_sync(1 + grp, kWarpsPerGroup * 32);
+    if (gw < 4) {
+      const int t = gw * 32 + lane;  // 0..127: one output each
+      const int l = t >> 2, j = t & 3;
       float sum = 0.f;
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) sum += reinterpret_cast<const float*>(&red[w * 32 + l])[j];
+      for (int w = 0; w < kWarpsPerGroup; ++w) sum += reinterpret_cast<const float*>(&gred[w * 32 + l])[j];
       const int row = (l >> 2) + 8 * (j >> 1);
       const int m = 2 * (l & 3) + (j & 1);
       const int64_t n = tile * kTileRows + row;
@@ -391,7 +430,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         }
       }
     }
-    named_bar_sync(1, kConsumerWarps * 32);
+    named_bar_sync(1 + grp, kWarpsPerGroup * 32);
   }
 }
 
@@ -445,27 +484,50 @@ __global__ void __launch_bounds__(256) gemv_generic(const MatArgs a) {
 
 // ------------------------------------------------------------- launch ----
 
+struct GemvPlan {
+  int chunk_groups = 0, chunks = 0, stages = 0, row_pitch = 0, x_pitch = 0;
+  size_t smem = 0;
+};
+
+// Largest chunk (preferably the whole row) and the most stages (>= 3, or
+// >= 2 for the largest rows) that fit the shared memory.
 template <int FMT>
-static size_t gemv_smem_bytes(const MatArgs& a, int stages, int* row_pitch, int* x_pitch, int* chunks) {
+static bool gemv_plan(const MatArgs& a, GemvPlan* out) {
   using F = GemvFmt<FMT>;
+  if (a.M < 1 || a.M > 8) return false;
   const int64_t gpr = a.K / F::kGroupK;
-  const int chunk_groups = static_cast<int>(std::min<int64_t>(kChunkGroups, gpr));
-  *chunks = static_cast<int>((gpr + kChunkGroups - 1) / kChunkGroups);
-  *row_pitch = ((chunk_groups * F::kGroupBytes + 15) / 16) * 16 + 16;  // +16: spreads banks, covers over-read
-  *x_pitch = static_cast<int>(a.K * 2 + 32);
-  return kBarrierBytes + kRedBytes + static_cast<size_t>(a.M) * (*x_pitch) +
-         static_cast<size_t>(stages) * kTileRows * (*row_pitch);
+  if (a.K % (static_cast<int64_t>(F::kGroupK) * F::kChunkAlign) != 0) return false;
+  const size_t avail = device_max_smem_optin();
+  const int64_t x_pitch = a.K * 2 + 32;
+  const size_t fixed = kBarrierBytes + kRedBytes + static_cast<size_t>(a.M) * x_pitch;
+  if (fixed >= avail) return false;
+  for (int min_stages : {3, 2}) {
+    int64_t cg = gpr;
+    while (cg >= F::kChunkAlign) {
+      const int64_t pitch = ((cg * F::kGroupBytes + 15) / 16) * 16 + 16;  // +16: bank spread, over-read room
+      const int64_t stage = kTileRows * pitch;
+      const int64_t fit = static_cast<int64_t>(avail - fixed) / stage;
+      if (fit >= min_stages) {
+        out->chunk_groups = static_cast<int>(cg);
+        out->chunks = static_cast<int>((gpr + cg - 1) / cg);
+        out->stages = static_cast<int>(std::min<int64_t>(fit, F::kMaxStages));
+        out->row_pitch = static_cast<int>(pitch);
+        out->x_pitch = static_cast<int>(x_pitch);
+        out->smem = fixed + static_cast<size_t>(out->stages) * stage;
+        return true;
+      }
+      // halve the chunk, keeping it a multiple of the alignment
+      cg = ((cg / 2) / F::kChunkAlign) * F::kChunkAlign;
+    }
+  }
+  return false;
 }
 
 template <int FMT>
 static bool gemv_fast_ok_t(const MatArgs& a) {
-  using F = GemvFmt<FMT>;
-  const int64_t align_k = static_cast<int64_t>(F::kGroupK) * F::kGroupAlign;
-  if (a.M < 1 || a.M > 8) return false;
-  if (a.K % align_k != 0) return false;
   if (reinterpret_cast<uintptr_t>(a.w) % 16 != 0 || a.w_stride % 16 != 0) return false;
-  int rp, xp, ch;
-  return gemv_smem_bytes<FMT>(a, 2, &rp, &xp, &ch) <= device_max_smem_optin();
+  GemvPlan plan;
+  return gemv_plan<FMT>(a, &plan);
 }
 
 bool gemv_fast_ok(const MatArgs& a) {
@@ -480,7 +542,8 @@ bool gemv_fast_ok(const MatArgs& a) {
 template <int FMT>
 static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream) {
   using F = GemvFmt<FMT>;
-  if (!gemv_fast_ok_t<FMT>(a)) {
+  GemvPlan plan;
+  if (reinterpret_cast<uintptr_t>(a.w) % 16 != 0 || a.w_stride % 16 != 0 || !gemv_plan<FMT>(a, &plan)) {
     const int64_t blocks = std::min<int64_t>((a.N + 7) / 8, int64_t(device_sm_count()) * 16);
     gemv_generic<FMT><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
     return cudaGetLastError();
@@ -498,17 +561,16 @@ static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream) {
   p.K = a.K;
   p.M = static_cast<int>(a.M);
   p.groups_per_row = a.K / F::kGroupK;
+  p.chunk_groups = plan.chunk_groups;
+  p.chunks_per_row = plan.chunks;
+  p.stages = plan.stages;
+  p.row_pitch = plan.row_pitch;
+  p.x_pitch = plan.x_pitch;
   p.y_bf16 = a.y_bf16;
   p.accumulate = a.accumulate;
   p.ftz = a.ftz;
-  p.x_vec16 = (reinterpret_cast<uintptr_t>(a.x) % 16 == 0) && (a.x_s8 * 2) % 16 == 0 && (a.x_sm * 2) % 16 == 0;
-  int stages = F::kStages;
-  size_t smem = 0;
-  for (; stages >= 2; --stages) {
-    smem = gemv_smem_bytes<FMT>(a, stages, &p.row_pitch, &p.x_pitch, &p.chunks_per_row);
-    if (smem <= device_max_smem_optin()) break;
-  }
-  p.stages = stages;
+  p.x_vec8 = (reinterpret_cast<uintptr_t>(a.x) % 8 == 0) && (a.x_s8 * 2) % 8 == 0 && (a.x_sm * 2) % 8 == 0;
+
   int dev = 0;
   cudaGetDevice(&dev);
   const int slot = FMT == kQ4_0 ? 0 : (FMT == kQ8_0 ? 1 : 2);
@@ -519,24 +581,10 @@ static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     configured[dev & 63][slot].store(true, std::memory_order_release);
   }
-  // Occupancy depends only on (device, format, dynamic smem); cache it so
-  // launches made under CUDA-graph capture issue no extra runtime calls.
-  static std::atomic<int64_t> occ_cache[64][3][8];
-  const int bucket = static_cast<int>(std::min<int64_t>(7, a.M - 1));
-  const int64_t key = (static_cast<int64_t>(smem) << 8);
-  int occ = 0;
-  const int64_t cached = occ_cache[dev & 63][slot][bucket].load(std::memory_order_relaxed);
-  if (cached != 0 && (cached & ~int64_t(0xff)) == key) {
-    occ = static_cast<int>(cached & 0xff);
-  } else {
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_kernel<FMT>, kGemvThreads, smem);
-    if (e != cudaSuccess) return e;
-    occ = std::max(occ, 1);
-    occ_cache[dev & 63][slot][bucket].store(key | occ, std::memory_order_relaxed);
-  }
+  // One CTA per SM: the stages fill the shared memory by design.
   const int64_t tiles = (a.N + kTileRows - 1) / kTileRows;
-  const int64_t grid = std::min<int64_t>(tiles, int64_t(device_sm_count()) * occ);
-  gemv_kernel<FMT><<<static_cast<unsigned>(grid), kGemvThreads, smem, stream>>>(p);
+  const int64_t grid = std::min<int64_t>(tiles, int64_t(device_sm_count()));
+  gemv_kernel<FMT><<<static_cast<unsigned>(grid), kGemvThreads, plan.smem, stream>>>(p);
   return cudaGetLastError();
 }
 

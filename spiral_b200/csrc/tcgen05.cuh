@@ -1,0 +1,113 @@
+// tcgen05.cuh — thin wrappers over the sm_100a tensor-core (tcgen05), tensor
+// memory (TMEM) and tensor-TMA instructions used by the dequant-GEMM.
+//
+// Conventions (PTX ISA 8.6+, sm_100a):
+//  * A TMEM address is (lane << 16) | column; an allocation returns the base.
+//  * For kind::f16 with cta_group::1 and M = 128, the D accumulator occupies
+//    lanes 0..127 (row m = lane m), one fp32 per column (column n = output
+//    column n).  An A operand taken from TMEM holds row m in lane m with two
+//    16-bit elements per 32-bit column: A[m][k] is column k/2, low half for
+//    even k.
+//  * A warp may only access the 32 TMEM lanes 32*(warp % 4) .. +31.
+//  * B comes from shared memory through a 64-bit matrix descriptor.
+#pragma once
+
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace spiral {
+namespace tc {
+
+// ---- TMEM allocation (one full warp executes these) ----------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// ---- ordering between tcgen05 operations and thread synchronization ------
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---- TMEM stores / loads (warp-collective, 32 lanes x N columns) ---------
+__device__ __forceinline__ void st_32x32b_x16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void ld_32x32b_x16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// ---- MMA ------------------------------------------------------------------
+// Instruction descriptor for kind::f16: bf16 A and B (both K-major), fp32 D.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
+  return (1u << 4)                               // D format: f32
+         | (1u << 7)                             // A format: bf16
+         | (1u << 10)                            // B format: bf16
+         | (static_cast<uint32_t>(N >> 3) << 17)  // N / 8
+         | (static_cast<uint32_t>(M >> 4) << 24);  // M / 16
+}
+
+// Shared-memory matrix descriptor: K-major operand in the canonical 128-byte
+// swizzle layout (rows of 128 bytes, 8-row atoms of 1024 bytes, 16-byte
+// chunks XOR-ed with row % 8), as a TMA tensor load with SWIZZLE_128B writes
+// it.  `addr` is the shared address of the first element of the K-slice (the
+// atom base is 1024-byte aligned; advancing K by 16 bf16 adds 32 bytes).
+__device__ __forceinline__ uint64_t sdesc_sw128_kmajor(uint32_t addr) {
+  const uint64_t start = (addr >> 4) & 0x3FFFu;
+  const uint64_t lbo = 1;                     // unused for swizzled K-major
+  const uint64_t sbo = 1024 >> 4;             // 8-row atom stride
+  return start | (lbo << 16) | (sbo << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, M=128, N from idesc, K=16.
+__device__ __forceinline__ void mma_ts(uint32_t d_taddr, uint32_t a_taddr, uint64_t b_desc, uint32_t idesc,
+                                       bool accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(d_taddr),
+      "r"(a_taddr), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation this thread issued so far has
+// completed.
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// ---- TMA tensor load (2-D tile, no multicast) ----------------------------
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int32_t c0, int32_t c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+}  // namespace tc
+}  // namespace spiral
