@@ -55,10 +55,11 @@ def parse_args(argv=None):
     ap.add_argument("--fmt", default="q4_0", choices=("q4_0", "q8_0", "q6_k"))
     ap.add_argument("--no-extras", action="store_true", help="skip the per-format / per-batch extras")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
-    ap.add_argument("--profile", choices=("gemv", "dequant"), default=None,
+    ap.add_argument("--profile", choices=("gemv", "dequant", "gemm"), default=None,
                     help="ncu helper: run --warmup + --steps eager launches of one kernel on one GPU "
                          "(B from --batch), nothing else")
-    ap.add_argument("--batch", type=int, default=1, help="activation vectors for --profile gemv")
+    ap.add_argument("--batch", type=int, default=1, help="activation vectors for --profile gemv / gemm")
+    ap.add_argument("--features", type=int, default=N_DIM, help="output features for --profile gemv / gemm")
     return ap.parse_args(argv)
 
 
@@ -72,11 +73,12 @@ def run_profile(args):
 
     torch.cuda.set_device(0)
     fid = F.BY_NAME[args.fmt]
-    K, N = K_DIM, (N_DIM if args.profile == "gemv" or args.fmt != "q4_0" else 4096)
+    K = K_DIM
+    N = args.features if args.profile in ("gemv", "gemm") else (N_DIM if args.fmt != "q4_0" else 4096)
     raw = F.generate(fid, K, N, seed=0)
     n = args.warmup + args.steps
     ws = [torch.from_numpy(raw).cuda() for _ in range(min(n, 8))]
-    if args.profile == "gemv":
+    if args.profile in ("gemv", "gemm"):
         x = torch.from_numpy(F.gen_activations(args.batch, K, seed=1).view(np.int16)).cuda().view(torch.bfloat16)
         y = torch.empty((args.batch, N), dtype=torch.bfloat16, device="cuda")
         for i in range(n):
@@ -460,7 +462,27 @@ def bench_extras(sp, F, dev, K, N, timed, graph_steps, hbm_peak):
     (config 0/1), each with its own rotating buffers and graphs."""
     import torch
 
-    out = {"gemv": {}, "dequant": {}}
+    out = {"gemv": {}, "dequant": {}, "gemm": {}}
+    _, tc_peak, _ = measured_peaks()
+    for name in ("q4_0", "q8_0"):
+        fid = F.BY_NAME[name]
+        for Ng in (4096, N):
+            rawg = F.generate(fid, K, Ng, seed=0)
+            wg = torch.from_numpy(rawg).to(dev)
+            for Mg in (512, 2048):
+                x = torch.from_numpy(F.gen_activations(Mg, K, seed=Mg).view(np.int16)).to(dev).view(torch.bfloat16)
+                y = torch.empty((Mg, Ng), dtype=torch.bfloat16, device=dev)
+
+                def body_g(i, wg=wg, x=x, y=y, fid=fid, Ng=Ng):
+                    sp.mul_mat(fid, wg, x, Ng, K, y, y_dtype=sp.BF16)
+
+                steps = 20
+                ms = timed(steps, 3, body_g, {})
+                t = ms / steps * 1e-3
+                fl = 2.0 * Mg * Ng * K
+                out["gemm"][f"{name}_M{Mg}_N{Ng}"] = {"us": t * 1e6, "TFLOPs": fl / t / 1e12,
+                                                       "frac_bf16_peak": fl / t / 1e12 / tc_peak}
+            del wg
     for name in ("q4_0", "q8_0", "q6_k"):
         fid = F.BY_NAME[name]
         rb = F.row_bytes(fid, K)

@@ -26,6 +26,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstring>
 #include <mutex>
 
 #include "api_internal.h"
@@ -52,6 +53,7 @@ struct GemmParams {
   int M, N, K;
   int y_bf16, accumulate, ftz;
   int token_blocks, feature_blocks;
+  int tma_store;  // bf16 output written through the staging tile + TMA store
 };
 
 // ------------------------------------------------------ weight dequant ----
@@ -149,7 +151,8 @@ struct ChunkDecoder<kQ8_0> {
 
 template <int FMT, int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmParams p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
+                const GemmParams p) {
   using CD = ChunkDecoder<FMT>;
   constexpr uint32_t kXStageBytes = BN * 128;
   constexpr uint32_t kIdesc = tc::idesc_bf16_f32(kGemmRows, BN);
@@ -157,7 +160,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // 1024-byte alignment for the swizzled activation ring
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xring = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kXStages * kXStageBytes);
+  uint16_t* ystage = reinterpret_cast<uint16_t*>(smem + kXStages * kXStageBytes);  // [BN][128] bf16
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kXStages * kXStageBytes + BN * kGemmRows * 2);
   uint64_t* x_full = bars;
   uint64_t* x_empty = bars + kXStages;
   uint64_t* a_full = bars + 2 * kXStages;
@@ -306,6 +310,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // --------------------------------------------------------- epilogue ----
     const int q = warp & 3;
     const int row = 32 * q + lane;
+    const int et = threadIdx.x - kWarpEpilogue0 * 32;  // 0..127
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q) << 16);
     uint32_t tcount = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tcount) {
       const int tb = t % p.token_blocks, fb = t / p.token_blocks;
@@ -313,33 +319,61 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc::fence_after_sync();
       const int n = fb * kGemmRows + row;
       const int m0 = tb * BN;
+      if (p.tma_store) {
+        // The previous tile's store must have finished reading the staging tile.
+        if (et == 0) tc::bulk_wait_read_all();
+        named_bar_sync(1, 128);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t v[16];
-        tc::ld_32x32b_x16(tmem + (static_cast<uint32_t>(32 * q) << 16) + c, v);
-        tc::wait_ld();
-        if (n < p.N) {
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tc::ld_32x32b_x32(trow + c, v);
+          tc::wait_ld();
+          if (c + 32 >= BN) {  // accumulator fully read: the next tile's MMAs may start
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d_empty);
+          }
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int m = m0 + c + i;
-            if (m < p.M) {
-              const float f = __uint_as_float(v[i]);
-              const int64_t off = static_cast<int64_t>(m) * p.y_stride + n;
-              if (p.y_bf16) {
-                static_cast<uint16_t*>(p.y)[off] = static_cast<uint16_t>(pack_bf16x2(f, 0.f) & 0xFFFFu);
-              } else if (p.accumulate) {
-                static_cast<float*>(p.y)[off] += f;
-              } else {
-                static_cast<float*>(p.y)[off] = f;
+          for (int i = 0; i < 32; ++i)
+            ystage[(c + i) * kGemmRows + row] =
+                static_cast<uint16_t>(pack_bf16x2(__uint_as_float(v[i]), 0.f) & 0xFFFFu);
+        }
+        tc::fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (et == 0) {
+          tc::tma_store_2d(&ymap, ystage, fb * kGemmRows, m0);
+          tc::bulk_commit_group();
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t v[16];
+          tc::ld_32x32b_x16(trow + c, v);
+          tc::wait_ld();
+          if (n < p.N) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int m = m0 + c + i;
+              if (m < p.M) {
+                const float f = __uint_as_float(v[i]);
+                const int64_t off = static_cast<int64_t>(m) * p.y_stride + n;
+                if (p.y_bf16) {
+                  static_cast<uint16_t*>(p.y)[off] = static_cast<uint16_t>(pack_bf16x2(f, 0.f) & 0xFFFFu);
+                } else if (p.accumulate) {
+                  static_cast<float*>(p.y)[off] += f;
+                } else {
+                  static_cast<float*>(p.y)[off] = f;
+                }
               }
             }
           }
         }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(d_empty);
       }
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(d_empty);
     }
+    if (et == 0) tc::bulk_wait_all();
   }
 
   tc::fence_before_sync();
@@ -367,7 +401,7 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 
 template <int BN>
 constexpr size_t gemm_smem() {
-  return 1024 /*alignment slack*/ + kXStages * BN * 128 + 256 /*barriers*/;
+  return 1024 /*alignment slack*/ + kXStages * BN * 128 + BN * kGemmRows * 2 /*y staging*/ + 256 /*barriers*/;
 }
 
 }  // namespace
@@ -393,7 +427,22 @@ static cudaError_t gemm_launch(const MatArgs& a, cudaStream_t stream) {
                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  // bf16 output: a TMA tensor store of each [BN][128] tile (clipped at M, N)
+  CUtensorMap ymap;
+  memset(&ymap, 0, sizeof(ymap));
+  const bool tma_store = a.y_bf16 && !a.accumulate && reinterpret_cast<uintptr_t>(a.y) % 16 == 0 &&
+                         (a.y_sm * 2) % 16 == 0;
+  if (tma_store) {
+    const cuuint64_t ydims[2] = {static_cast<cuuint64_t>(a.N), static_cast<cuuint64_t>(a.M)};
+    const cuuint64_t ystrides[1] = {static_cast<cuuint64_t>(a.y_sm * 2)};
+    const cuuint32_t ybox[2] = {kGemmRows, BN};
+    const CUresult ry = get_encode()(&ymap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.y, ydims, ystrides, ybox, estr,
+                                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (ry != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  }
   GemmParams p{};
+  p.tma_store = tma_store ? 1 : 0;
   p.w = a.w;
   p.w_stride = a.w_stride;
   p.y = a.y;
@@ -418,7 +467,7 @@ static cudaError_t gemm_launch(const MatArgs& a, cudaStream_t stream) {
   }
   const int tiles = p.token_blocks * p.feature_blocks;
   const int grid = std::min(tiles, device_sm_count());
-  gemm_kernel<FMT, BN><<<grid, kGemmThreads, smem, stream>>>(map, p);
+  gemm_kernel<FMT, BN><<<grid, kGemmThreads, smem, stream>>>(map, ymap, p);
   return cudaGetLastError();
 }
 
