@@ -82,7 +82,7 @@ def run_profile(args):
         x = torch.from_numpy(F.gen_activations(args.batch, K, seed=1).view(np.int16)).cuda().view(torch.bfloat16)
         y = torch.empty((args.batch, N), dtype=torch.bfloat16, device="cuda")
         for i in range(n):
-            sp.mul_mat(fid, ws[i % len(ws)], x, N, K, y, y_dtype=sp.BF16)
+            sp.mul_mat(fid, ws[i % len(ws)], x, N, K, y, y_dtype=sp.BF16, static_weights=True)
     else:
         out = torch.empty((N, K), dtype=torch.bfloat16, device="cuda")
         for i in range(n):
@@ -294,21 +294,25 @@ def run_spiral(args):
     ys = {B: torch.empty((B, Nr), dtype=torch.bfloat16, device=dev) for B in BATCHES}
     yg = {B: torch.empty((world, B, Nr), dtype=torch.bfloat16, device=dev) for B in BATCHES} if world > 1 else None
 
+    # every MUL_MAT of the sweep reads a different weight copy, so no launch
+    # finds its weights in L2 (the last use of a copy is `copies` launches ago)
     def sweep(i, x=None, y=None):
-        w = weights[i % copies]
-        for B in BATCHES:
+        for j, B in enumerate(BATCHES):
+            w = weights[(i * len(BATCHES) + j) % copies]
             xb = xs[B] if x is None else x[B]
             yb = ys[B] if y is None else y[B]
-            sp.mul_mat(fid, w, xb, Nr, K, yb, y_dtype=sp.BF16)
+            sp.mul_mat(fid, w, xb, Nr, K, yb, y_dtype=sp.BF16, static_weights=True)
             if world > 1:
                 dist.all_gather_into_tensor(yg[B], yb)
 
-    # warm-up (also configures kernel attributes before any capture)
+    stream = torch.cuda.Stream(device=dev)
+    # warm-up (also configures kernel attributes and the per-stream GEMV
+    # scratch before any capture; graphs are captured on `stream`)
     for i in range(3):
         sweep(i)
+    with torch.cuda.stream(stream):
+        sweep(0)
     torch.cuda.synchronize()
-
-    stream = torch.cuda.Stream(device=dev)
     graph_steps = copies if copies <= 64 else 64
 
     def capture(nsteps, start, body):
@@ -369,9 +373,9 @@ def run_spiral(args):
         cache_k = {}
 
         def sweep_local(i):
-            w = weights[i % copies]
-            for B in BATCHES:
-                sp.mul_mat(fid, w, xs[B], Nr, K, ys[B], y_dtype=sp.BF16)
+            for j, B in enumerate(BATCHES):
+                w = weights[(i * len(BATCHES) + j) % copies]
+                sp.mul_mat(fid, w, xs[B], Nr, K, ys[B], y_dtype=sp.BF16, static_weights=True)
 
         msk = timed(max(graph_steps, args.steps // 4), 3, sweep_local, cache_k)
         alg = sum(rb * Nr + B * K * 2 + B * Nr * 2 for B in BATCHES)
@@ -388,10 +392,10 @@ def run_spiral(args):
     xd = {B: torch.empty((B, K), dtype=torch.bfloat16, device=dev) for B in BATCHES}
 
     def sweep_e2e(i):
-        w = weights[i % copies]
-        for B in BATCHES:
+        for j, B in enumerate(BATCHES):
+            w = weights[(i * len(BATCHES) + j) % copies]
             xd[B].view(torch.int16).copy_(hx[B], non_blocking=True)
-            sp.mul_mat(fid, w, xd[B], Nr, K, ys[B], y_dtype=sp.BF16)
+            sp.mul_mat(fid, w, xd[B], Nr, K, ys[B], y_dtype=sp.BF16, static_weights=True)
             if world > 1:
                 dist.all_gather_into_tensor(yg[B], ys[B])
                 hy[B].view(B, N).copy_(yg[B].permute(1, 0, 2).reshape(B, N).view(torch.int16), non_blocking=True)
@@ -495,7 +499,7 @@ def bench_extras(sp, F, dev, K, N, timed, graph_steps, hbm_peak):
             y = torch.empty((B, N), dtype=torch.bfloat16, device=dev)
 
             def body(i, ws=ws, x=x, y=y, fid=fid, copies=copies):
-                sp.mul_mat(fid, ws[i % copies], x, N, K, y, y_dtype=sp.BF16)
+                sp.mul_mat(fid, ws[i % copies], x, N, K, y, y_dtype=sp.BF16, static_weights=True)
 
             steps = graph_steps * 20
             ms = timed(steps, 3, body, {})

@@ -79,6 +79,11 @@ typedef enum spiral_status {
 /* Flags (bit set). */
 #define SPIRAL_FLAG_FTZ_SCALES 0x1u  /* flush subnormal fp16 scales to +0      */
 #define SPIRAL_FLAG_ACCUMULATE 0x2u  /* mul_mat: dst += result (f32 dst only)  */
+/* mul_mat, M <= 8: the weights are not written by the kernel queued just
+ * before this call on the stream (true for inference weights), so the GEMV
+ * may start streaming them while that kernel finishes.  Activations are
+ * always read, and outputs written, only after the preceding kernel ends. */
+#define SPIRAL_FLAG_STATIC_WEIGHTS 0x4u
 
 /* ---------------------------------------------------------------- info --- */
 
@@ -178,7 +183,10 @@ SPIRAL_API int spiral_quants_unpack_all(int fmt, const void* packed, void* weigh
  * x_row_stride_elems; y: M rows of N at y_row_stride_elems.
  * M <= 8 runs the fused dequant-GEMV (decode); larger M runs the tcgen05
  * dequant-GEMM (prefill).  Results are within fp32-summation-order error of
- * the reference's dequant-then-fp32-matmul (src/quants/tests/mmul.py:104-121).
+ * the reference's dequant-then-fp32-matmul (src/quants/tests/mmul.py:104-121)
+ * and identical from run to run (fixed summation order).  Nothing is
+ * allocated.  The GEMV is launched with programmatic stream serialization
+ * so that the next kernel on the stream can be scheduled while it finishes.
  */
 SPIRAL_API int spiral_mul_mat(int fmt, const void* w, int64_t w_row_stride_bytes,
                    const void* x, int64_t x_row_stride_elems, void* y,

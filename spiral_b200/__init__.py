@@ -23,6 +23,7 @@ Q4_0, Q8_0, Q6_K = 2, 8, 14
 F32, BF16 = 0, 30
 FLAG_FTZ_SCALES = 0x1
 FLAG_ACCUMULATE = 0x2
+FLAG_STATIC_WEIGHTS = 0x4
 FORMATS = {"q4_0": Q4_0, "q8_0": Q8_0, "q6_k": Q6_K}
 BLOCK_K = {Q4_0: 32, Q8_0: 32, Q6_K: 256}
 BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q6_K: 210}
@@ -166,8 +167,11 @@ def unpack_all(fmt, packed, weights_rows: int, weights_cols: int, out=None, *, f
 
 def mul_mat(fmt, w, x, N: int, K: int, y=None, *, y_dtype: int = BF16, w_row_stride: int | None = None,
             x_row_stride: int | None = None, y_row_stride: int | None = None, accumulate: bool = False,
-            ftz: bool = False, stream=None, M: int | None = None):
-    """ggml MUL_MAT: y[m][n] = sum_k bf16(W[n][k]) * x[m][k] (fp32 accumulate)."""
+            ftz: bool = False, stream=None, M: int | None = None, static_weights: bool = False):
+    """ggml MUL_MAT: y[m][n] = sum_k bf16(W[n][k]) * x[m][k] (fp32 accumulate).
+
+    static_weights: the weights are not written by the kernel queued just
+    before on the stream, so the decode GEMV may start streaming them early."""
     f = fmt_id(fmt)
     if M is None:
         M = int(x.shape[0])
@@ -175,7 +179,8 @@ def mul_mat(fmt, w, x, N: int, K: int, y=None, *, y_dtype: int = BF16, w_row_str
         import torch
 
         y = torch.empty((M, N), dtype=torch.bfloat16 if y_dtype == BF16 else torch.float32, device=x.device)
-    flags = (FLAG_FTZ_SCALES if ftz else 0) | (FLAG_ACCUMULATE if accumulate else 0)
+    flags = ((FLAG_FTZ_SCALES if ftz else 0) | (FLAG_ACCUMULATE if accumulate else 0)
+             | (FLAG_STATIC_WEIGHTS if static_weights else 0))
     _check(lib().spiral_mul_mat(f, _ptr(w), w_row_stride or row_bytes(f, K), _ptr(x), x_row_stride or K, _ptr(y),
                                 y_dtype, y_row_stride or N, M, N, K, flags, _stream(stream)))
     return y

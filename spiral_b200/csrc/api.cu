@@ -255,6 +255,7 @@ int spiral_mul_mat(int fmt, const void* w, int64_t w_row_stride_bytes, const voi
   a.y_bf16 = y_dtype == SPIRAL_DTYPE_BF16;
   a.accumulate = (flags & SPIRAL_FLAG_ACCUMULATE) != 0;
   a.ftz = (flags & SPIRAL_FLAG_FTZ_SCALES) != 0;
+  a.static_weights = (flags & SPIRAL_FLAG_STATIC_WEIGHTS) != 0;
   a.M = M;
   a.N = N;
   a.K = K;

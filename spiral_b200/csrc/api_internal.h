@@ -33,6 +33,7 @@ struct MatArgs {
   bool y_bf16;
   bool accumulate;
   bool ftz;
+  bool static_weights;  // weights are not written by the preceding kernel
   int64_t M, N, K;
 };
 

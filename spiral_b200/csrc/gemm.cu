@@ -30,8 +30,10 @@
 #include <mutex>
 
 #include "api_internal.h"
+#include "chunk_decode.cuh"
 #include "decode.cuh"
 #include "tcgen05.cuh"
+#include "tma_host.h"
 
 namespace spiral {
 
@@ -61,34 +63,6 @@ struct GemmParams {
 template <int FMT>
 struct ChunkDecoder;
 
-__device__ __forceinline__ uint32_t fma2_pack_gemm(uint32_t fa, uint32_t fb, uint64_t D2, uint64_t C2) {
-  const uint64_t in = (static_cast<uint64_t>(fb) << 32) | fa;
-  uint64_t out;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(out) : "l"(in), "l"(D2), "l"(C2));
-  return pack_bf16x2(__uint_as_float(static_cast<uint32_t>(out)), __uint_as_float(static_cast<uint32_t>(out >> 32)));
-}
-__device__ __forceinline__ uint64_t dup2f(float v) {
-  const uint64_t b = __float_as_uint(v);
-  return (b << 32) | b;
-}
-template <int I>
-__device__ __forceinline__ uint32_t b2f1(uint32_t w) {
-  return __byte_perm(w, 0x3F800000u, 0x7604u | (I << 4));
-}
-// Bytes [o, o+4) of a register image of 16-byte loads, o even.
-template <int O>
-__device__ __forceinline__ uint32_t word_at(const uint32_t* R) {
-  if constexpr ((O & 3) == 0) {
-    return R[O >> 2];
-  } else {
-    return __funnelshift_r(R[O >> 2], R[(O >> 2) + 1], 16);
-  }
-}
-template <int O>
-__device__ __forceinline__ uint32_t half_at(const uint32_t* R) {
-  return (R[O >> 2] >> ((O & 3) * 8)) & 0xFFFFu;
-}
-
 // Q4_0: a 256-weight chunk of one row is 8 blocks (144 bytes).  Half h takes
 // blocks 4h..4h+3; its bytes [72h, 72h+72) lie in the 16-byte aligned window
 // [64h, 64h+80).
@@ -99,19 +73,7 @@ struct ChunkDecoder<kQ4_0> {
   __device__ __forceinline__ static int64_t window(int h) { return 64 * h; }
   template <int H, int J>
   __device__ __forceinline__ static void block(const uint32_t* R, bool ftz, uint32_t (&out)[16]) {
-    constexpr int O = 8 * H + 18 * J;  // block start within the window
-    const float d = fp16_bits_to_f32(half_at<O>(R), ftz);
-    const uint64_t DL = dup2f(d * 32768.0f), CL = dup2f(d * -32776.0f);
-    const uint64_t DH = dup2f(d * 2048.0f), CH = dup2f(d * -2056.0f);
-    const uint32_t q[4] = {word_at<O + 2>(R), word_at<O + 6>(R), word_at<O + 10>(R), word_at<O + 14>(R)};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t L = q[i] & 0x0F0F0F0Fu, Hn = q[i] & 0xF0F0F0F0u;
-      out[2 * i] = fma2_pack_gemm(b2f1<0>(L), b2f1<1>(L), DL, CL);      // weights 4i, 4i+1
-      out[2 * i + 1] = fma2_pack_gemm(b2f1<2>(L), b2f1<3>(L), DL, CL);  // 4i+2, 4i+3
-      out[8 + 2 * i] = fma2_pack_gemm(b2f1<0>(Hn), b2f1<1>(Hn), DH, CH);  // 16+4i, ...
-      out[9 + 2 * i] = fma2_pack_gemm(b2f1<2>(Hn), b2f1<3>(Hn), DH, CH);
-    }
+    BlockDecoder<kQ4_0>::block<8 * H + 18 * J>(R, ftz, out);
   }
 };
 
@@ -124,26 +86,7 @@ struct ChunkDecoder<kQ8_0> {
   __device__ __forceinline__ static int64_t window(int h) { return 128 * h; }
   template <int H, int J>
   __device__ __forceinline__ static void block(const uint32_t* R, bool ftz, uint32_t (&out)[16]) {
-    constexpr int O = 8 * H + 34 * J;
-    const float d = fp16_bits_to_f32(half_at<O>(R), ftz);
-    const uint64_t D = dup2f(d * 32768.0f), C = dup2f(d * -32896.0f);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      uint32_t q;
-      switch (i) {  // compile-time offsets
-        case 0: q = word_at<O + 2>(R); break;
-        case 1: q = word_at<O + 6>(R); break;
-        case 2: q = word_at<O + 10>(R); break;
-        case 3: q = word_at<O + 14>(R); break;
-        case 4: q = word_at<O + 18>(R); break;
-        case 5: q = word_at<O + 22>(R); break;
-        case 6: q = word_at<O + 26>(R); break;
-        default: q = word_at<O + 30>(R); break;
-      }
-      q ^= 0x80808080u;
-      out[2 * i] = fma2_pack_gemm(b2f1<0>(q), b2f1<1>(q), D, C);
-      out[2 * i + 1] = fma2_pack_gemm(b2f1<2>(q), b2f1<3>(q), D, C);
-    }
+    BlockDecoder<kQ8_0>::block<8 * H + 34 * J>(R, ftz, out);
   }
 };
 
@@ -386,19 +329,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 namespace {
 
-PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
 template <int BN>
 constexpr size_t gemm_smem() {
   return 1024 /*alignment slack*/ + kXStages * BN * 128 + BN * kGemmRows * 2 /*y staging*/ + 256 /*barriers*/;
@@ -413,7 +343,7 @@ bool gemm_supported(const MatArgs& a) {
   if (a.M > (int64_t(1) << 30) || a.N > (int64_t(1) << 30)) return false;
   if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0 || (a.x_sm * 2) % 16 != 0) return false;
   if (reinterpret_cast<uintptr_t>(a.w) % 16 != 0 || a.w_stride % 16 != 0) return false;
-  return get_encode() != nullptr;
+  return tensor_map_encoder() != nullptr;
 }
 
 template <int FMT, int BN>
@@ -423,7 +353,7 @@ static cudaError_t gemm_launch(const MatArgs& a, cudaStream_t stream) {
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.x_sm * 2)};
   const cuuint32_t box[2] = {kXSliceK, BN};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = get_encode()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a.x), dims, strides,
+  const CUresult r = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a.x), dims, strides,
                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
@@ -436,7 +366,7 @@ static cudaError_t gemm_launch(const MatArgs& a, cudaStream_t stream) {
     const cuuint64_t ydims[2] = {static_cast<cuuint64_t>(a.N), static_cast<cuuint64_t>(a.M)};
     const cuuint64_t ystrides[1] = {static_cast<cuuint64_t>(a.y_sm * 2)};
     const cuuint32_t ybox[2] = {kGemmRows, BN};
-    const CUresult ry = get_encode()(&ymap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.y, ydims, ystrides, ybox, estr,
+    const CUresult ry = tensor_map_encoder()(&ymap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.y, ydims, ystrides, ybox, estr,
                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (ry != CUDA_SUCCESS) return cudaErrorInvalidValue;

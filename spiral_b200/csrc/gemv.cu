@@ -23,6 +23,11 @@
 //    permuted to match each lane's A fragment, so a B fragment is one 8-byte
 //    shared load.  The MMA contracts over k, so permuting k identically in A
 //    and B leaves the sum unchanged.
+//  * Programmatic dependent launch: each CTA lets the next kernel on the
+//    stream launch at once, and reads activations / writes outputs only after
+//    griddepcontrol.wait (the preceding kernel has completed).  With
+//    SPIRAL_FLAG_STATIC_WEIGHTS the producer streams weights before that
+//    wait, so this launch's ramp-up overlaps the previous kernel's tail.
 //
 // Dequantization (exact): a quant byte is placed in the mantissa of an fp32
 // with one byte permute, f = 1 + q*2^-s, and one fused multiply-add computes
@@ -78,10 +83,16 @@ struct GemvParams {
   int stages;
   int row_pitch;  // bytes per row slot in a stage
   int x_pitch;    // bytes per activation vector in the permuted copy
-  int y_bf16, accumulate, ftz, x_vec8;
+  int y_bf16, accumulate, ftz;
+  int static_weights;  // weights may be read before the preceding grid ends
 };
 
 // ------------------------------------------------------------- helpers ---
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 __device__ __forceinline__ void mma_bf16_16816(float (&acc)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
@@ -277,31 +288,71 @@ struct GroupDecoder<kQ6_K> {
 
 // ------------------------------------------------- activation staging ----
 
-__device__ __forceinline__ uint2 load_x4(const GemvParams& p, int m, int64_t k) {
-  const uint16_t* base = p.x + (k >> 3) * p.x_s8 + static_cast<int64_t>(m) * p.x_sm + (k & 7);
-  if (p.x_vec8) return *reinterpret_cast<const uint2*>(base);  // k % 4 == 0
-  return make_uint2(base[0] | (static_cast<uint32_t>(base[1]) << 16),
-                    base[2] | (static_cast<uint32_t>(base[3]) << 16));
-}
-
 // Permuted activations: entry (m, group g, step s, lane column c) holds the
 // 4 consecutive k that lane column c contracts at that step, at
 //   xs + m*x_pitch + (g*kSteps + s)*32 + c*8.
+// Fast path (contiguous 16-byte aligned rows, K <= kRawK): every thread loads
+// its 16-byte pieces of all M rows at once (one L2 round trip), then row by
+// row the raw copy goes through `raw` (the idle reduction buffer) and is
+// permuted from there.  Otherwise each entry gathers from global memory.
+constexpr int kRawK = kRedBytes / 2;
+constexpr int kStageThreads = kConsumerWarps * 32;
+constexpr int kRawPieces = (kRawK / 8 + kStageThreads - 1) / kStageThreads;
+
 template <int FMT>
-__device__ void stage_x(const GemvParams& p, uint8_t* xs, int tid, int nthreads) {
+__device__ void stage_x(const GemvParams& p, uint8_t* xs, uint8_t* raw, int tid) {
   using F = GemvFmt<FMT>;
-  const int64_t groups = p.K / F::kGroupK;
-  const int64_t per_m = groups * F::kSteps * 4;
-  const int64_t entries = static_cast<int64_t>(p.M) * per_m;
-  for (int64_t e = tid; e < entries; e += nthreads) {
+  constexpr int kStepShift = F::kSteps == 8 ? 3 : 4;
+  const int per_m = static_cast<int>(p.K / F::kGroupK) * F::kSteps * 4;
+  const bool fast = p.x_s8 == 8 && p.K <= kRawK && (reinterpret_cast<uintptr_t>(p.x) & 15u) == 0 &&
+                    (p.x_sm & 7) == 0;
+  if (fast) {
+    const int pieces = static_cast<int>(p.K / 8);  // 16-byte pieces per row
+    uint4 v[8][kRawPieces];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+#pragma unroll
+      for (int i = 0; i < kRawPieces; ++i) {
+        const int q = tid + i * kStageThreads;
+        if (m < p.M && q < pieces)
+          v[m][i] = __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(m) * p.x_sm) + q);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      if (m < p.M) {
+#pragma unroll
+        for (int i = 0; i < kRawPieces; ++i) {
+          const int q = tid + i * kStageThreads;
+          if (q < pieces) reinterpret_cast<uint4*>(raw)[q] = v[m][i];
+        }
+        named_bar_sync(kGroupsPerCta + 1, kStageThreads);
+        const uint16_t* xr = reinterpret_cast<const uint16_t*>(raw);
+        uint8_t* dst = xs + static_cast<int64_t>(m) * p.x_pitch;
+        for (int e = tid; e < per_m; e += kStageThreads) {
+          const int c = e & 3, gs = e >> 2, st = gs & (F::kSteps - 1), g = gs >> kStepShift;
+          const int k = g * F::kGroupK + GroupDecoder<FMT>::xk(st, c);
+          *reinterpret_cast<uint2*>(dst + gs * 32 + c * 8) =
+              make_uint2(xr[k] | (static_cast<uint32_t>(xr[k + 1]) << 16),
+                         xr[k + 2] | (static_cast<uint32_t>(xr[k + 3]) << 16));
+        }
+        named_bar_sync(kGroupsPerCta + 1, kStageThreads);
+      }
+    }
+    return;
+  }
+  const int64_t total = static_cast<int64_t>(p.M) * per_m;
+  for (int64_t e = tid; e < total; e += kStageThreads) {
     const int m = static_cast<int>(e / per_m);
-    const int64_t rem = e - m * per_m;
-    const int c = static_cast<int>(rem & 3);
-    const int64_t gs = rem >> 2;  // g*kSteps + s
-    const int64_t g = gs / F::kSteps;
-    const int s = static_cast<int>(gs - g * F::kSteps);
-    const int64_t k = g * F::kGroupK + GroupDecoder<FMT>::xk(s, c);
-    *reinterpret_cast<uint2*>(xs + static_cast<int64_t>(m) * p.x_pitch + gs * 32 + c * 8) = load_x4(p, m, k);
+    const int em = static_cast<int>(e - static_cast<int64_t>(m) * per_m);
+    const int c = em & 3, gs = em >> 2, st = gs & (F::kSteps - 1), g = gs >> kStepShift;
+    const int64_t k = static_cast<int64_t>(g) * F::kGroupK + GroupDecoder<FMT>::xk(st, c);
+    const uint16_t* base = p.x + static_cast<int64_t>(m) * p.x_sm;
+    uint32_t v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = base[((k + j) >> 3) * p.x_s8 + ((k + j) & 7)];
+    *reinterpret_cast<uint2*>(xs + static_cast<int64_t>(m) * p.x_pitch + gs * 32 + c * 8) =
+        make_uint2(v[0] | (v[1] << 16), v[2] | (v[3] << 16));
   }
 }
 
@@ -331,12 +382,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     }
     abort_flag = 0;
     fence_mbar_init();
+    griddep_launch_dependents();
   }
   __syncthreads();
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------- producer ----
     if (lane == 0) {
+      if (!p.static_weights) griddep_wait();
       const uint64_t pol = l2_evict_first_policy();
       uint32_t it = 0;
       for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
@@ -368,7 +421,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
   }
 
   // --------------------------------------------------------- consumers -----
-  stage_x<FMT>(p, xs, threadIdx.x, kConsumerWarps * 32);
+  griddep_wait();  // activations may come from the preceding kernel
+  stage_x<FMT>(p, xs, reinterpret_cast<uint8_t*>(red), threadIdx.x);
   named_bar_sync(kGroupsPerCta + 1, kConsumerWarps * 32);
 
   const int grp = warp / kWarpsPerGroup, gw = warp % kWarpsPerGroup;
@@ -569,7 +623,7 @@ static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream) {
   p.y_bf16 = a.y_bf16;
   p.accumulate = a.accumulate;
   p.ftz = a.ftz;
-  p.x_vec8 = (reinterpret_cast<uintptr_t>(a.x) % 8 == 0) && (a.x_s8 * 2) % 8 == 0 && (a.x_sm * 2) % 8 == 0;
+  p.static_weights = a.static_weights;
 
   int dev = 0;
   cudaGetDevice(&dev);
@@ -584,8 +638,17 @@ static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream) {
   // One CTA per SM: the stages fill the shared memory by design.
   const int64_t tiles = (a.N + kTileRows - 1) / kTileRows;
   const int64_t grid = std::min<int64_t>(tiles, int64_t(device_sm_count()));
-  gemv_kernel<FMT><<<static_cast<unsigned>(grid), kGemvThreads, plan.smem, stream>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<FMT>, p);
 }
 
 cudaError_t gemv(const MatArgs& a, cudaStream_t stream) {

@@ -127,3 +127,97 @@ def test_gemv_is_deterministic(cuda, big_weights):
     b = sp.mul_mat(F.Q4_0, w, x, N, K, y_dtype=sp.F32).cpu().numpy()
     assert np.array_equal(a, b)
     assert sp.device_status() == 0
+
+
+@pytest.mark.parametrize("fid", FMTS, ids=lambda f: F.NAMES[f])
+@pytest.mark.parametrize(
+    "M,N",
+    [
+        (1, 16),  # one tile
+        (3, 1792),  # 112 tiles < SMs: the 8-way row shard of config 2
+        (8, 4112),  # 257 tiles
+        (2, 300),  # partial last tile
+    ],
+)
+def test_gemv_small_and_ragged_tile_counts(cuda, fid, M, N):
+    """Tile counts below, above and not a multiple of the SM count; bitwise
+    repeatable, and the same bits with the early weight stream enabled."""
+    K = 4096
+    raw = F.generate(fid, K, N, seed=N + 3)
+    x = F.gen_activations(M, K, seed=M + 5)
+    ref = oracle.mul_mat_f64(fid, raw, x, K, N)
+    w, xd = dev_bytes(raw), dev_bf16(x)
+    a = sp.mul_mat(fid, w, xd, N, K, y_dtype=sp.F32).cpu().numpy()
+    ok, rel = tolerance_ok(a, ref, bf16_out=False)
+    assert ok, rel
+    b = sp.mul_mat(fid, w, xd, N, K, y_dtype=sp.F32, static_weights=True).cpu().numpy()
+    assert np.array_equal(a, b)
+    assert sp.device_status() == 0
+
+
+def test_gemv_back_to_back_shapes(cuda):
+    """Consecutive GEMVs of different shapes and formats on one stream, with
+    programmatic dependent launch between them, each match the oracle."""
+    import torch
+
+    K = 4096
+    cases = [(F.Q4_0, 1, 4112), (F.Q8_0, 8, 16), (F.Q6_K, 2, 1792), (F.Q4_0, 5, 300)]
+    data = []
+    for i, (fid, M, N) in enumerate(cases):
+        raw = F.generate(fid, K, N, seed=40 + i)
+        x = F.gen_activations(M, K, seed=50 + i)
+        y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        data.append((fid, M, N, raw, x, dev_bytes(raw), dev_bf16(x), y))
+    for _ in range(2):
+        for fid, M, N, raw, x, w, xd, y in data:
+            sp.mul_mat(fid, w, xd, N, K, y, y_dtype=sp.F32, static_weights=True)
+    torch.cuda.synchronize()
+    for fid, M, N, raw, x, w, xd, y in data:
+        ok, rel = tolerance_ok(y.cpu().numpy(), oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=False)
+        assert ok, (F.NAMES[fid], M, N, rel)
+    assert sp.device_status() == 0
+
+
+def test_gemv_in_cuda_graph_on_fresh_stream(cuda):
+    """Captured into a CUDA graph on a fresh stream, replays match the
+    oracle."""
+    import torch
+
+    fid, M, N, K = F.Q4_0, 4, 4112, 4096
+    raw = F.generate(fid, K, N, seed=9)
+    x = F.gen_activations(M, K, seed=10)
+    w, xd = dev_bytes(raw), dev_bf16(x)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        sp.mul_mat(fid, w, xd, N, K, y, y_dtype=sp.F32, static_weights=True, stream=s)
+    for _ in range(3):
+        y.zero_()
+        g.replay()
+    torch.cuda.synchronize()
+    ok, rel = tolerance_ok(y.cpu().numpy(), oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=False)
+    assert ok, rel
+    del g
+    assert sp.device_status() == 0
+
+
+@pytest.mark.parametrize("fid", FMTS, ids=lambda f: F.NAMES[f])
+@pytest.mark.parametrize("M,N,K,x_off", [(1, 300, 4096, 1), (8, 4112, 4096, 1), (3, 1792, 6144, 0), (8, 33, 8192, 0)])
+def test_gemv_unaligned_activations_and_long_k(cuda, fid, M, N, K, x_off):
+    """Activations only 2-byte aligned (staged by gathers) and K above the
+    fast staging limit."""
+    if K % F.BLOCK_K[fid]:
+        pytest.skip("K not a block multiple")
+    import torch
+
+    raw = F.generate(fid, K, N, seed=K + N + x_off)
+    x = F.gen_activations(M, K, seed=M + 77)
+    xbuf = np.zeros(M * K + x_off, dtype=np.uint16)
+    xbuf[x_off:] = x.reshape(-1)
+    xd = dev_bf16(xbuf)[x_off:].view(M, K)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    sp.mul_mat(fid, dev_bytes(raw), xd, N, K, y, y_dtype=sp.F32, static_weights=True)
+    ok, rel = tolerance_ok(y.cpu().numpy(), oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=False)
+    assert ok, rel
+    assert sp.device_status() == 0
