@@ -468,7 +468,7 @@ def bench_extras(sp, F, dev, K, N, timed, graph_steps, hbm_peak):
 
     out = {"gemv": {}, "dequant": {}, "gemm": {}}
     _, tc_peak, _ = measured_peaks()
-    for name in ("q4_0", "q8_0"):
+    for name in ("q4_0", "q8_0", "q6_k"):
         fid = F.BY_NAME[name]
         for Ng in (4096, N):
             rawg = F.generate(fid, K, Ng, seed=0)

@@ -90,4 +90,89 @@ struct BlockDecoder<kQ8_0> {
   }
 };
 
+// Q6_K super-block half H (weights 128H .. 128H+127) for one feature row,
+// read straight from global memory.  The super-block starts P bytes past a
+// 16-byte boundary (P even; 210-byte blocks in 16-byte aligned rows), so the
+// loads are 16-byte aligned windows and every field offset is compile-time:
+//   ql[64H .. 64H+64)  -> window bytes [64H, 64H+80),  5 loads
+//   qh[32H .. 32H+32)  -> [128+32H, 176+32H),           3 loads
+//   sc[8H .. 8H+8), d  -> [192, 224),                   2 loads
+// (relative to the super-block start minus P).  The windows may run up to 14
+// bytes past the super-block; with rows a multiple of 8 super-blocks the last
+// super-block of a row has P = 14 and every window ends inside the row.
+// Output: 4 sub-blocks s (weights 128H + 32s + l, l < 32) as 16 bf16x2 words
+// each, weight (q6 - 32) * (d * sc[8H + 2s + l/16]) with
+// q6 = (ql[64H + 32(s&1) + l] >> 4(s>>1)) & 15 | ((qh[32H + l] >> 2s) & 3) << 4
+// (src/quants/tests/formats/q6_k.py:55-97).  With bit 7 set the byte lands in
+// an fp32 mantissa as f = 1 + q6 * 2^-7, and f * (128 ds) - 160 ds =
+// (q6 - 32) ds exactly (ds = d * sc has at most 18 significant bits).
+template <int P, int H>
+struct Q6KHalf {
+  template <int O>
+  __device__ __forceinline__ static uint32_t byte_at(const uint32_t* R) {
+    return (R[O >> 2] >> ((O & 3) * 8)) & 0xFFu;
+  }
+  template <int I>
+  __device__ __forceinline__ static uint32_t b2f2(uint32_t w) {
+    return __byte_perm(w, 0x3F000000u, 0x7054u | (I << 8));
+  }
+  // Emits the half's 4 sub-blocks through store(j, out[16]).
+  template <typename Store>
+  __device__ __forceinline__ static void run(const uint8_t* sb, bool ftz, Store&& store) {
+    const uint8_t* win = sb - P;
+    uint32_t Rl[20], Rh[12], Rs[8];
+    const uint4* pl = reinterpret_cast<const uint4*>(win + 64 * H);
+    const uint4* ph = reinterpret_cast<const uint4*>(win + 128 + 32 * H);
+    const uint4* ps = reinterpret_cast<const uint4*>(win + 192);
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+      const uint4 v = __ldg(pl + i);
+      Rl[4 * i] = v.x; Rl[4 * i + 1] = v.y; Rl[4 * i + 2] = v.z; Rl[4 * i + 3] = v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      const uint4 v = __ldg(ph + i);
+      Rh[4 * i] = v.x; Rh[4 * i + 1] = v.y; Rh[4 * i + 2] = v.z; Rh[4 * i + 3] = v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint4 v = __ldg(ps + i);
+      Rs[4 * i] = v.x; Rs[4 * i + 1] = v.y; Rs[4 * i + 2] = v.z; Rs[4 * i + 3] = v.w;
+    }
+    const float d = fp16_bits_to_f32(half_at<P + 16>(Rs), ftz);
+    sub<0>(Rl, Rh, Rs, d, store);
+    sub<1>(Rl, Rh, Rs, d, store);
+    sub<2>(Rl, Rh, Rs, d, store);
+    sub<3>(Rl, Rh, Rs, d, store);
+  }
+  template <int S, typename Store>
+  __device__ __forceinline__ static void sub(const uint32_t* Rl, const uint32_t* Rh, const uint32_t* Rs, float d,
+                                             Store& store) {
+    const float ds0 = d * static_cast<float>(static_cast<int8_t>(byte_at<P + 8 * H + 2 * S>(Rs)));
+    const float ds1 = d * static_cast<float>(static_cast<int8_t>(byte_at<P + 8 * H + 2 * S + 1>(Rs)));
+    const uint64_t D0 = dup2f(ds0 * 128.0f), C0 = dup2f(ds0 * -160.0f);
+    const uint64_t D1 = dup2f(ds1 * 128.0f), C1 = dup2f(ds1 * -160.0f);
+    uint32_t out[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      uint32_t ql, qh;
+      switch (i) {  // compile-time offsets
+        case 0: ql = word_at<P + 32 * (S & 1) + 0>(Rl); qh = word_at<P + 0>(Rh); break;
+        case 1: ql = word_at<P + 32 * (S & 1) + 4>(Rl); qh = word_at<P + 4>(Rh); break;
+        case 2: ql = word_at<P + 32 * (S & 1) + 8>(Rl); qh = word_at<P + 8>(Rh); break;
+        case 3: ql = word_at<P + 32 * (S & 1) + 12>(Rl); qh = word_at<P + 12>(Rh); break;
+        case 4: ql = word_at<P + 32 * (S & 1) + 16>(Rl); qh = word_at<P + 16>(Rh); break;
+        case 5: ql = word_at<P + 32 * (S & 1) + 20>(Rl); qh = word_at<P + 20>(Rh); break;
+        case 6: ql = word_at<P + 32 * (S & 1) + 24>(Rl); qh = word_at<P + 24>(Rh); break;
+        default: ql = word_at<P + 32 * (S & 1) + 28>(Rl); qh = word_at<P + 28>(Rh); break;
+      }
+      const uint32_t q = ((ql >> (4 * (S >> 1))) & 0x0F0F0F0Fu) | (((qh >> (2 * S)) & 0x03030303u) << 4) | 0x80808080u;
+      const uint64_t D = i < 4 ? D0 : D1, C = i < 4 ? C0 : C1;
+      out[2 * i] = fma2_pack_bf16(b2f2<0>(q), b2f2<1>(q), D, C);
+      out[2 * i + 1] = fma2_pack_bf16(b2f2<2>(q), b2f2<3>(q), D, C);
+    }
+    store(S, out);
+  }
+};
+
 }  // namespace spiral

@@ -90,6 +90,30 @@ struct ChunkDecoder<kQ8_0> {
   }
 };
 
+// Q6_K: a 256-weight chunk of one row is one 210-byte super-block; half h
+// takes weights [128h, 128h + 128) (Q6KHalf, compile-time offsets for each
+// of the 8 possible 16-byte phases of the super-block start).
+template <>
+struct ChunkDecoder<kQ6_K> {
+  static constexpr int kChunkBytes = 210;
+  static constexpr int kLoads = 1;  // unused: Q6KHalf loads its own windows
+  __device__ __forceinline__ static int64_t window(int) { return 0; }
+};
+
+template <int H, typename Store>
+__device__ __forceinline__ void q6k_half_any_phase(const uint8_t* sb, int phase, bool ftz, Store&& store) {
+  switch (phase) {
+    case 0: Q6KHalf<0, H>::run(sb, ftz, store); break;
+    case 2: Q6KHalf<2, H>::run(sb, ftz, store); break;
+    case 4: Q6KHalf<4, H>::run(sb, ftz, store); break;
+    case 6: Q6KHalf<6, H>::run(sb, ftz, store); break;
+    case 8: Q6KHalf<8, H>::run(sb, ftz, store); break;
+    case 10: Q6KHalf<10, H>::run(sb, ftz, store); break;
+    case 12: Q6KHalf<12, H>::run(sb, ftz, store); break;
+    default: Q6KHalf<14, H>::run(sb, ftz, store); break;
+  }
+}
+
 // ------------------------------------------------------------- kernel -----
 
 template <int FMT, int BN>
@@ -210,6 +234,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int n = fb * kGemmRows + row;
       const bool valid = n < p.N;
       const uint8_t* wrow = p.w + static_cast<int64_t>(valid ? n : 0) * p.w_stride;
+      if constexpr (FMT == kQ6_K) {
+        for (int kc = 0; kc < kchunks; ++kc, ++ait) {
+          const int s = ait % kAStages;
+          if (!wait(&a_empty[s], ((ait / kAStages) & 1u) ^ 1u)) break;
+          tc::fence_after_sync();
+          const uint32_t tbase = tmem + (static_cast<uint32_t>(32 * q) << 16) + kAColBase + s * kAStageCols + 64 * h;
+          auto store = [&](int j, const uint32_t (&out)[16]) { tc::st_32x32b_x16(tbase + 16 * j, out); };
+          // Every lane runs the same path (tcgen05.st is warp-collective): rows
+          // past N decode row 0 and their outputs are never stored.  The
+          // phase is warp-uniform (16-byte aligned base and row stride).
+          const uint8_t* sb = wrow + static_cast<int64_t>(kc) * CD::kChunkBytes;
+          const int phase = static_cast<int>(reinterpret_cast<uintptr_t>(sb) & 15u);
+          if (h == 0)
+            q6k_half_any_phase<0>(sb, phase, p.ftz, store);
+          else
+            q6k_half_any_phase<1>(sb, phase, p.ftz, store);
+          tc::wait_st();
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[s]);
+        }
+      } else {
       for (int kc = 0; kc < kchunks; ++kc, ++ait) {
         const int s = ait % kAStages;
         uint32_t R[CD::kLoads * 4];
@@ -246,6 +292,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[s]);
+      }
       }
       if (*abortv) break;
     }
@@ -337,7 +384,9 @@ constexpr size_t gemm_smem() {
 }  // namespace
 
 bool gemm_supported(const MatArgs& a) {
-  if (a.fmt != kQ4_0 && a.fmt != kQ8_0) return false;
+  if (a.fmt != kQ4_0 && a.fmt != kQ8_0 && a.fmt != kQ6_K) return false;
+  // Q6_K: rows of whole 8-super-block runs keep its 16-byte windows in bounds
+  if (a.fmt == kQ6_K && a.K % 2048 != 0) return false;
   if (a.x_s8 != 8 || a.y_s8 != 8) return false;  // row-major operands only
   if (a.K % kChunkK != 0 || a.K > (int64_t(1) << 30)) return false;
   if (a.M > (int64_t(1) << 30) || a.N > (int64_t(1) << 30)) return false;
@@ -405,6 +454,7 @@ cudaError_t gemm(const MatArgs& a, cudaStream_t stream) {
   switch (a.fmt) {
     case kQ4_0: return gemm_launch<kQ4_0, 256>(a, stream);
     case kQ8_0: return gemm_launch<kQ8_0, 256>(a, stream);
+    case kQ6_K: return gemm_launch<kQ6_K, 256>(a, stream);
   }
   return cudaErrorInvalidValue;
 }

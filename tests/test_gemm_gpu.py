@@ -18,7 +18,7 @@ from oracle import formats as F
 from .gpu_util import dev_bf16, dev_bytes, host_bits, tolerance_ok
 
 pytestmark = pytest.mark.gpu
-GEMM_FMTS = [F.Q4_0, F.Q8_0]
+GEMM_FMTS = [F.Q4_0, F.Q8_0, F.Q6_K]
 
 
 @pytest.mark.parametrize("fid", GEMM_FMTS, ids=lambda f: F.NAMES[f])
@@ -32,6 +32,8 @@ GEMM_FMTS = [F.Q4_0, F.Q8_0]
     ],
 )
 def test_gemm_small_exact_shapes(cuda, fid, M, N, K):
+    if K % F.BLOCK_K[fid]:
+        pytest.skip("K not a block multiple")
     raw = F.generate(fid, K, N, seed=M + N + K)
     x = F.gen_activations(M, K, seed=K)
     ref = oracle.mul_mat_f64(fid, raw, x, K, N)
@@ -82,4 +84,26 @@ def test_gemm_accumulate_and_strided_output(cuda):
     ok, rel = tolerance_ok(got[:, :N], ref, bf16_out=False)
     assert ok, rel
     assert np.all(got[:, N:] == 1.0)
+    assert sp.device_status() == 0
+
+
+@pytest.mark.parametrize(
+    "M,N,K",
+    [
+        (256, 128, 2048),  # one tile, 8 super-blocks per row (all 8 start phases)
+        (300, 200, 4096),  # partial token and feature blocks
+        (16, 130, 6144),
+    ],
+)
+def test_gemm_q6_k_tensor_core_path(cuda, M, N, K):
+    """Q6_K through the tcgen05 GEMM (K a multiple of 2048: rows of whole
+    8-super-block runs), every 16-byte phase of a super-block start."""
+    fid = F.Q6_K
+    raw = F.generate(fid, K, N, seed=M + N + K)
+    x = F.gen_activations(M, K, seed=K + 1)
+    ref = oracle.mul_mat_f64(fid, raw, x, K, N)
+    y = sp.mul_mat(fid, dev_bytes(raw), dev_bf16(x), N, K, y_dtype=sp.F32).cpu().numpy()
+    ok, rel = tolerance_ok(y, ref, bf16_out=False)
+    assert ok, rel
+    assert rel < 5e-5, rel  # fp32 accumulation over K up to 6144
     assert sp.device_status() == 0
