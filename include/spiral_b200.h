@@ -209,6 +209,38 @@ SPIRAL_API int spiral_quants_unpack_mmul_all(int fmt, const void* packed,
                                   int64_t inputs_vecs, unsigned flags,
                                   void* stream);
 
+/* ------------------------------------------------------------ MoE FFN ---- */
+
+/* Bytes of scratch spiral_moe_ffn needs for these dims (0 if invalid).  The
+ * caller allocates it once (device memory, 256-byte aligned) and may reuse it
+ * for every call with the same or smaller dims on one stream. */
+SPIRAL_API int64_t spiral_moe_workspace_bytes(int64_t n_experts_local, int64_t hidden,
+                                              int64_t inter, int64_t tokens, int64_t topk);
+
+/* MoE FFN decode layer with quantized SwiGLU experts (the
+ * reference has no MoE operator — this is the expert FFN built from its
+ * quantized MUL_MAT, src/quants/q4_0/mmul.aie.h:16-90):
+ *   for each token t and slot j < topk with global expert id e = ids[t][j]
+ *   in [expert_first, expert_first + n_experts_local):
+ *     h = bf16( silu(x_t Wg_e^T) * (x_t Wu_e^T) )       (inter values)
+ *     y_t += weights[t][j] * (h Wd_e^T)                  (hidden values)
+ *   accumulated in fp32, summed over slots in order j = 0..topk-1, stored as
+ *   y_dtype (BF16 rounds once; F32 with SPIRAL_FLAG_ACCUMULATE adds into y).
+ * Ids outside the local range (or negative) are skipped, so expert-parallel
+ * ranks each produce their partial y and combine them.
+ * w_gate, w_up: n_experts_local x [inter rows][hidden] canonical tensors,
+ * back to back; w_down: n_experts_local x [hidden rows][inter].  Rows dense
+ * (row bytes = K / block * block bytes).  hidden and inter multiples of 256
+ * (Q6_K: 2048), hidden <= 4096, inter <= 2048.  x: [tokens][x_row_stride]
+ * bf16, 16-byte aligned rows.  ids int32 / weights f32: [tokens][topk]. */
+SPIRAL_API int spiral_moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w_down,
+                              int64_t n_experts_local, int64_t expert_first, int64_t hidden,
+                              int64_t inter, const void* x, int64_t x_row_stride_elems,
+                              int64_t tokens, const int32_t* expert_ids,
+                              const float* expert_weights, int64_t topk, void* y, int y_dtype,
+                              int64_t y_row_stride_elems, void* workspace,
+                              int64_t workspace_bytes, unsigned flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -103,3 +103,46 @@ def mul_mat_f32(fmt: int, raw: np.ndarray, x_bits: np.ndarray, K: int, N: int, f
     lib().oracle_mul_mat_f32(fmt, _ptr(raw), row_bytes(fmt, K), _ptr(x), x.shape[1], _ptr(y), M, N, K, int(ftz),
                              threads)
     return y
+
+
+def _bf16_round(a: np.ndarray) -> np.ndarray:
+    from ml_dtypes import bfloat16
+
+    return a.astype(np.float32).astype(bfloat16).astype(np.float64)
+
+
+def moe_ffn_f64(fmt: int, w_gate: np.ndarray, w_up: np.ndarray, w_down: np.ndarray, x_bits: np.ndarray,
+                ids: np.ndarray, weights: np.ndarray, hidden: int, inter: int, n_experts_local: int,
+                expert_first: int = 0, ftz: bool = False) -> np.ndarray:
+    """Reference MoE FFN in float64 over bf16-dequantized experts:
+    y[t] = sum_j w[t][j] * Wd_e (bf16(silu(Wg_e x_t) * (Wu_e x_t))), h rounded to
+    bf16 through float32 (as the device rounds an fp32 h), local experts only,
+    slots summed in order.  Dequantizes one expert at a time."""
+    from .formats import bf16_bits_to_f32, row_bytes
+
+    T, topk = ids.shape
+    x = bf16_bits_to_f32(x_bits).astype(np.float64)
+    y = np.zeros((T, hidden), dtype=np.float64)
+    gu_bytes = inter * row_bytes(fmt, hidden)
+    d_bytes = hidden * row_bytes(fmt, inter)
+    contrib = {}
+    for e in sorted(set(int(v) for v in ids.reshape(-1))):
+        le = e - expert_first
+        if le < 0 or le >= n_experts_local:
+            continue
+        slots = [(t, j) for t in range(T) for j in range(topk) if ids[t, j] == e]
+        wg = bf16_bits_to_f32(dequant_bf16(fmt, w_gate[le * gu_bytes:(le + 1) * gu_bytes], hidden, inter, ftz)).astype(np.float64)
+        wu = bf16_bits_to_f32(dequant_bf16(fmt, w_up[le * gu_bytes:(le + 1) * gu_bytes], hidden, inter, ftz)).astype(np.float64)
+        wd = bf16_bits_to_f32(dequant_bf16(fmt, w_down[le * d_bytes:(le + 1) * d_bytes], inter, hidden, ftz)).astype(np.float64)
+        xs = x[[t for t, _ in slots]]
+        g = xs @ wg.T
+        u = xs @ wu.T
+        h = _bf16_round(g / (1.0 + np.exp(-g)) * u)
+        out = h @ wd.T
+        for (t, j), row in zip(slots, out):
+            contrib[(t, j)] = float(weights[t, j]) * row
+    for t in range(T):
+        for j in range(topk):
+            if (t, j) in contrib:
+                y[t] += contrib[(t, j)]
+    return y

@@ -192,3 +192,21 @@ def mul_mat_f64(fmt, raw, x_bits: np.ndarray, K: int, N: int, ftz: bool = False)
     w = bf16_bits_to_f32(dequant_bf16(fmt, raw, K, N, ftz)).astype(np.float64)
     x = bf16_bits_to_f32(x_bits).astype(np.float64)
     return x @ w.T
+
+
+
+def gen_routing(T: int, n_experts: int, topk: int, seed: int):
+    """BASELINE config 4 routing: per token topk distinct expert ids drawn
+    uniformly, weights = softmax over topk N(0,1) logits (float32)."""
+    rng = np.random.default_rng(seed)
+    ids = np.stack([rng.choice(n_experts, size=topk, replace=False) for _ in range(T)]).astype(np.int32)
+    logits = rng.standard_normal((T, topk))
+    w = np.exp(logits - logits.max(axis=1, keepdims=True))
+    w = (w / w.sum(axis=1, keepdims=True)).astype(np.float32)
+    return ids, w
+
+
+def gen_experts(fid: int, n_experts: int, rows: int, K: int, seed: int) -> np.ndarray:
+    """n_experts canonical [rows][K] tensors back to back (BASELINE
+    distributions)."""
+    return np.concatenate([generate(fid, K, rows, seed=seed * 1000 + e) for e in range(n_experts)])

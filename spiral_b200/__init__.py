@@ -44,6 +44,9 @@ _SIGNATURES = {
     "spiral_quants_unpack_all": ([_i32, _vp, _vp, _i64, _i64, _u32, _vp], _i32),
     "spiral_mul_mat": ([_i32, _vp, _i64, _vp, _i64, _vp, _i32, _i64, _i64, _i64, _i64, _u32, _vp], _i32),
     "spiral_quants_unpack_mmul_all": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _u32, _vp], _i32),
+    "spiral_moe_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64], _i64),
+    "spiral_moe_ffn": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i32,
+                        _i64, _vp, _i64, _u32, _vp], _i32),
 }
 
 _lib = None
@@ -193,3 +196,35 @@ def unpack_mmul_all(fmt, packed, inputs_tiled, outputs, weights_rows: int, weigh
                                                weights_rows, weights_cols, inputs_vecs,
                                                FLAG_FTZ_SCALES if ftz else 0, _stream(stream)))
     return outputs
+
+
+# ---------------------------------------------------------------- MoE FFN
+
+
+def moe_workspace_bytes(n_experts_local: int, hidden: int, inter: int, tokens: int, topk: int) -> int:
+    return lib().spiral_moe_workspace_bytes(n_experts_local, hidden, inter, tokens, topk)
+
+
+def moe_ffn(fmt, w_gate, w_up, w_down, x, expert_ids, expert_weights, *, hidden: int, inter: int,
+            n_experts_local: int, expert_first: int = 0, y=None, y_dtype: int = BF16, workspace=None,
+            accumulate: bool = False, ftz: bool = False, stream=None):
+    """MoE FFN decode layer (SwiGLU experts, quantized gate/up/down):
+    y[t] (+)= sum_j w[t][j] * down_e(bf16(silu(gate_e x_t) * up_e x_t)) over the
+    slots j whose expert e = ids[t][j] lies in [expert_first,
+    expert_first + n_experts_local).  x: [T][hidden] bf16; ids int32 and
+    weights f32: [T][topk]."""
+    import torch
+
+    f = fmt_id(fmt)
+    T, topk = int(expert_ids.shape[0]), int(expert_ids.shape[1])
+    if y is None:
+        y = torch.empty((T, hidden), dtype=torch.bfloat16 if y_dtype == BF16 else torch.float32, device=x.device)
+    need = moe_workspace_bytes(n_experts_local, hidden, inter, T, topk)
+    if workspace is None:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+    flags = (FLAG_FTZ_SCALES if ftz else 0) | (FLAG_ACCUMULATE if accumulate else 0)
+    _check(lib().spiral_moe_ffn(f, _ptr(w_gate), _ptr(w_up), _ptr(w_down), n_experts_local, expert_first, hidden,
+                                inter, _ptr(x), int(x.stride(0)), T, _ptr(expert_ids), _ptr(expert_weights), topk,
+                                _ptr(y), y_dtype, int(y.stride(0)), _ptr(workspace), int(workspace.numel()),
+                                flags, _stream(stream)))
+    return y

@@ -294,6 +294,54 @@ int spiral_quants_unpack_mmul_all(int fmt, const void* packed, const void* input
   return run_mat(a, static_cast<cudaStream_t>(stream));
 }
 
+int64_t spiral_moe_workspace_bytes(int64_t n_experts_local, int64_t hidden, int64_t inter, int64_t tokens,
+                                   int64_t topk) {
+  if (n_experts_local <= 0 || hidden <= 0 || inter <= 0 || tokens <= 0 || topk <= 0) return 0;
+  if (tokens > (int64_t(1) << 24) || topk > 64 || n_experts_local > 4096) return 0;
+  return static_cast<int64_t>(moe_workspace_bytes(n_experts_local, hidden, inter, tokens, topk));
+}
+
+int spiral_moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w_down, int64_t n_experts_local,
+                   int64_t expert_first, int64_t hidden, int64_t inter, const void* x, int64_t x_row_stride_elems,
+                   int64_t tokens, const int32_t* expert_ids, const float* expert_weights, int64_t topk, void* y,
+                   int y_dtype, int64_t y_row_stride_elems, void* workspace, int64_t workspace_bytes, unsigned flags,
+                   void* stream) {
+  g_last_error[0] = 0;
+  if (!fmt_valid(fmt)) return fail(SPIRAL_ERR_INVALID_FORMAT, "unknown quantized format %d", fmt);
+  if (n_experts_local <= 0 || expert_first < 0 || tokens <= 0 || topk <= 0 || topk > 64 || hidden <= 0 ||
+      inter <= 0 || n_experts_local > 4096 || tokens > (int64_t(1) << 24))
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "bad MoE dims (experts %lld, tokens %lld, topk %lld)",
+                (long long)n_experts_local, (long long)tokens, (long long)topk);
+  if (!moe_shape_ok(fmt, hidden, inter))
+    return fail(SPIRAL_ERR_INVALID_SHAPE,
+                "hidden=%lld / inter=%lld: need multiples of %d, hidden <= 4096 and inter <= 2048",
+                (long long)hidden, (long long)inter, fmt == SPIRAL_QFMT_Q6_K ? 2048 : 256);
+  if (!w_gate || !w_up || !w_down || !x || !expert_ids || !expert_weights || !y || !workspace)
+    return fail(SPIRAL_ERR_NULL_POINTER, "null MoE operand");
+  if (y_dtype != SPIRAL_DTYPE_BF16 && y_dtype != SPIRAL_DTYPE_F32)
+    return fail(SPIRAL_ERR_INVALID_ARGUMENT, "y_dtype %d is neither F32 nor BF16", y_dtype);
+  if ((flags & SPIRAL_FLAG_ACCUMULATE) && y_dtype != SPIRAL_DTYPE_F32)
+    return fail(SPIRAL_ERR_INVALID_ARGUMENT, "ACCUMULATE needs an F32 destination");
+  if (x_row_stride_elems < hidden || y_row_stride_elems < hidden)
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "x/y row strides smaller than hidden");
+  const auto al = [](const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
+  if (!al(w_gate, 16) || !al(w_up, 16) || !al(w_down, 16) || !al(x, 16) || (x_row_stride_elems % 8) != 0 ||
+      !al(expert_ids, 4) || !al(expert_weights, 4) || !al(workspace, 256) ||
+      !al(y, y_dtype == SPIRAL_DTYPE_F32 ? 4 : 2))
+    return fail(SPIRAL_ERR_ALIGNMENT, "MoE operands misaligned (weights, x rows 16 B; workspace 256 B)");
+  const int64_t need = spiral_moe_workspace_bytes(n_experts_local, hidden, inter, tokens, topk);
+  if (workspace_bytes < need)
+    return fail(SPIRAL_ERR_CAPACITY, "workspace %lld bytes < %lld needed", (long long)workspace_bytes,
+                (long long)need);
+  const cudaError_t e =
+      moe_ffn(fmt, w_gate, w_up, w_down, x, x_row_stride_elems, expert_ids, expert_weights, y, y_row_stride_elems,
+              y_dtype == SPIRAL_DTYPE_BF16, (flags & SPIRAL_FLAG_ACCUMULATE) != 0,
+              (flags & SPIRAL_FLAG_FTZ_SCALES) != 0, tokens, topk, hidden, inter, expert_first, n_experts_local,
+              workspace, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "moe launch");
+  return SPIRAL_OK;
+}
+
 int spiral_device_status(void* stream, uint32_t* code) {
   g_last_error[0] = 0;
   if (code == nullptr) return fail(SPIRAL_ERR_NULL_POINTER, "null code");

@@ -45,6 +45,14 @@ cudaError_t gemv(const MatArgs& a, cudaStream_t stream);
 bool gemm_supported(const MatArgs& a);
 cudaError_t gemm(const MatArgs& a, cudaStream_t stream);
 
+// moe.cu — MoE FFN decode layer over quantized experts.
+size_t moe_workspace_bytes(int64_t E_local, int64_t H, int64_t I, int64_t T, int64_t topk);
+bool moe_shape_ok(int fmt, int64_t H, int64_t I);
+cudaError_t moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w_down, const void* x,
+                    int64_t x_stride, const int32_t* ids, const float* wts, void* y, int64_t y_stride, bool y_bf16,
+                    bool accumulate, bool ftz, int64_t T, int64_t topk, int64_t H, int64_t I, int64_t e0,
+                    int64_t E_local, void* ws, cudaStream_t stream);
+
 // Device properties cached per device.
 int device_sm_count();
 size_t device_max_smem_optin();

@@ -1,0 +1,232 @@
+// gemv_decode.cuh — register-level decoders that feed mma.sync.m16n8k16 A
+// fragments straight from canonical GGUF blocks in shared memory, shared by
+// the decode GEMV (gemv.cu) and the MoE expert GEMVs (moe.cu).
+//
+// Dequantization is exact: a quant byte is placed in the mantissa of an fp32
+// with one byte permute, f = 1 + q*2^-s, and one fused multiply-add computes
+// f*(2^s*d) - (2^s + bias)*d = (q - bias)*d.  Both constants are exact in
+// fp32 (at most 24 significant bits) and so is the result, so the FMA does
+// not round; cvt.rn.bf16x2.f32 then rounds once to nearest even.  The A
+// fragments therefore hold exactly the bf16 weights of the standalone
+// dequant (bf16_rne(d*int), up to the sign of a zero weight, which cannot
+// change a dot product).  Pairs of weights go through one fma.rn.f32x2.
+#pragma once
+
+#include "common.cuh"
+
+namespace spiral {
+
+template <int FMT> struct GemvFmt;
+// kGroupK weights per group (the unit a consumer warp decodes); kSteps MMA
+// k-steps per group; a chunk must be a multiple of kChunkAlign groups to stay
+// 16-byte aligned.
+template <> struct GemvFmt<kQ4_0> {
+  static constexpr int kGroupK = 128, kGroupBytes = 72, kSteps = 8, kChunkAlign = 2, kMaxStages = 4;
+};
+template <> struct GemvFmt<kQ8_0> {
+  static constexpr int kGroupK = 128, kGroupBytes = 136, kSteps = 8, kChunkAlign = 2, kMaxStages = 4;
+};
+template <> struct GemvFmt<kQ6_K> {
+  static constexpr int kGroupK = 256, kGroupBytes = 210, kSteps = 16, kChunkAlign = 8, kMaxStages = 4;
+};
+
+// ------------------------------------------------------------- helpers ---
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&acc)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(acc[0]), "+f"(acc[1]), "+f"(acc[2]), "+f"(acc[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// Two fp32 bit patterns through one exact fma.rn.f32x2 with (D, C), then one
+// RNE pack to bf16x2 (fa in the low half).
+__device__ __forceinline__ uint32_t fma2_pack(uint32_t fa, uint32_t fb, uint64_t D2, uint64_t C2) {
+  const uint64_t in = (static_cast<uint64_t>(fb) << 32) | fa;
+  uint64_t out;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(out) : "l"(in), "l"(D2), "l"(C2));
+  return pack_bf16x2(__uint_as_float(static_cast<uint32_t>(out)), __uint_as_float(static_cast<uint32_t>(out >> 32)));
+}
+__device__ __forceinline__ uint64_t dup2(float v) {
+  const uint64_t b = __float_as_uint(v);
+  return (b << 32) | b;
+}
+
+// Byte i of w into bits 8..15 of 0x3F80_00_00: f = 1 + byte * 2^-15.
+template <int I>
+__device__ __forceinline__ uint32_t byte_to_f1(uint32_t w) {
+  return __byte_perm(w, 0x3F800000u, 0x7604u | (I << 4));
+}
+// Byte i of w (its bit 7 set) into bits 16..23 of 0x3F_00_00_00:
+// f = 1 + (byte & 0x7f) * 2^-7.
+template <int I>
+__device__ __forceinline__ uint32_t byte_to_f2(uint32_t w) {
+  return __byte_perm(w, 0x3F000000u, 0x7054u | (I << 8));
+}
+
+// --------------------------------------------- per-format group decoders --
+// ra / rb: this lane's two feature rows (r and r + 8) at the group start in
+// the stage (4-byte aligned for Q4_0/Q8_0, 2-byte for Q6_K); c = lane % 4;
+// xg = this lane's B-fragment column at step 0 of the group in the permuted
+// activations (stride 32 bytes per step).  xk(s, c) gives the k offset
+// (within the group) of the 4 consecutive weights lane column c contracts at
+// step s; the activation staging uses it to build the permuted copy.
+
+template <int FMT>
+struct GroupDecoder;
+
+// Q4_0: lane c owns block c of the 4-block group (18 bytes at 18c).  Step
+// 2j covers the low nibbles of qs word j (weights 4j..4j+3), step 2j+1 the
+// high nibbles (weights 16+4j..16+4j+3).
+template <>
+struct GroupDecoder<kQ4_0> {
+  __device__ __forceinline__ static void run(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg, bool ftz,
+                                             float (&acc)[4]) {
+    // qs starts at 18c + 2: 4-byte aligned for odd c, 2 mod 4 for even c.
+    const int woff = 18 * c + 2 * (c & 1);
+    const uint32_t sh = (c & 1) ? 0u : 16u;
+    uint32_t qa[4], qb[4];
+    {
+      uint32_t wa[5], wb[5];
+#pragma unroll
+      for (int i = 0; i < 5; ++i) {
+        wa[i] = lds32(ra + woff + 4 * i);
+        wb[i] = lds32(rb + woff + 4 * i);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        qa[j] = __funnelshift_r(wa[j], wa[j + 1], sh);
+        qb[j] = __funnelshift_r(wb[j], wb[j + 1], sh);
+      }
+    }
+    const float da = fp16_bits_to_f32(lds_u16(ra + 18 * c), ftz);
+    const float db = fp16_bits_to_f32(lds_u16(rb + 18 * c), ftz);
+    // low nibble: f = 1 + q 2^-15; high nibble (16q in the byte): 1 + q 2^-11.
+    // 2^15 + 8 = 8 * 4097 and 2^11 + 8 = 8 * 257 keep the bias products exact.
+    const uint64_t DLa = dup2(da * 32768.0f), CLa = dup2(da * -32776.0f);
+    const uint64_t DHa = dup2(da * 2048.0f), CHa = dup2(da * -2056.0f);
+    const uint64_t DLb = dup2(db * 32768.0f), CLb = dup2(db * -32776.0f);
+    const uint64_t DHb = dup2(db * 2048.0f), CHb = dup2(db * -2056.0f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t la = qa[j] & 0x0F0F0F0Fu, ha = qa[j] & 0xF0F0F0F0u;
+      const uint32_t lb = qb[j] & 0x0F0F0F0Fu, hb = qb[j] & 0xF0F0F0F0u;
+      const uint2 b0 = *reinterpret_cast<const uint2*>(xg + 32 * (2 * j));
+      mma_bf16_16816(acc, fma2_pack(byte_to_f1<0>(la), byte_to_f1<1>(la), DLa, CLa),
+                     fma2_pack(byte_to_f1<0>(lb), byte_to_f1<1>(lb), DLb, CLb),
+                     fma2_pack(byte_to_f1<2>(la), byte_to_f1<3>(la), DLa, CLa),
+                     fma2_pack(byte_to_f1<2>(lb), byte_to_f1<3>(lb), DLb, CLb), b0.x, b0.y);
+      const uint2 b1 = *reinterpret_cast<const uint2*>(xg + 32 * (2 * j + 1));
+      mma_bf16_16816(acc, fma2_pack(byte_to_f1<0>(ha), byte_to_f1<1>(ha), DHa, CHa),
+                     fma2_pack(byte_to_f1<0>(hb), byte_to_f1<1>(hb), DHb, CHb),
+                     fma2_pack(byte_to_f1<2>(ha), byte_to_f1<3>(ha), DHa, CHa),
+                     fma2_pack(byte_to_f1<2>(hb), byte_to_f1<3>(hb), DHb, CHb), b1.x, b1.y);
+    }
+  }
+  __host__ __device__ __forceinline__ static int xk(int s, int c) { return 32 * c + 16 * (s & 1) + 4 * (s >> 1); }
+};
+
+// Q8_0: lane c owns block c (34 bytes at 34c); step s = weights 4s..4s+3.
+// int8 q is biased to u = q + 128 (x ^ 0x80); f = 1 + u 2^-15 and
+// 2^15 + 128 = 128 * 257 keeps the bias product exact.
+template <>
+struct GroupDecoder<kQ8_0> {
+  __device__ __forceinline__ static void run(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg, bool ftz,
+                                             float (&acc)[4]) {
+    const int woff = 34 * c + 2 * (c & 1);
+    const uint32_t sh = (c & 1) ? 0u : 16u;
+    const float da = fp16_bits_to_f32(lds_u16(ra + 34 * c), ftz);
+    const float db = fp16_bits_to_f32(lds_u16(rb + 34 * c), ftz);
+    const uint64_t Da = dup2(da * 32768.0f), Ca = dup2(da * -32896.0f);
+    const uint64_t Db = dup2(db * 32768.0f), Cb = dup2(db * -32896.0f);
+    uint32_t pa = lds32(ra + woff), pb = lds32(rb + woff);
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      const uint32_t na = lds32(ra + woff + 4 * (s + 1)), nb = lds32(rb + woff + 4 * (s + 1));
+      const uint32_t qa = __funnelshift_r(pa, na, sh) ^ 0x80808080u;
+      const uint32_t qb = __funnelshift_r(pb, nb, sh) ^ 0x80808080u;
+      pa = na;
+      pb = nb;
+      const uint2 b = *reinterpret_cast<const uint2*>(xg + 32 * s);
+      mma_bf16_16816(acc, fma2_pack(byte_to_f1<0>(qa), byte_to_f1<1>(qa), Da, Ca),
+                     fma2_pack(byte_to_f1<0>(qb), byte_to_f1<1>(qb), Db, Cb),
+                     fma2_pack(byte_to_f1<2>(qa), byte_to_f1<3>(qa), Da, Ca),
+                     fma2_pack(byte_to_f1<2>(qb), byte_to_f1<3>(qb), Db, Cb), b.x, b.y);
+    }
+  }
+  __host__ __device__ __forceinline__ static int xk(int s, int c) { return 32 * c + 4 * s; }
+};
+
+// Q6_K: one super-block per group; lane c owns l in [8c, 8c+8) of both
+// halves.  Step t = 8h + 4*half + s covers y = 128h + 32s + 8c + 4*half + 0..3.
+// The 6-bit quant with bit 7 set gives f = 1 + q6 2^-7;
+// f*(128 ds) - 160 ds = (q6 - 32) ds with ds = d*sc (exact, <= 18 bits).
+template <>
+struct GroupDecoder<kQ6_K> {
+  // 8 bytes at p (p % 4 == sh/8 for a 2-byte aligned super-block start).
+  __device__ __forceinline__ static void load8(const uint8_t* p, uint32_t sh, uint32_t& lo, uint32_t& hi) {
+    const uint8_t* a = p - (sh >> 3);
+    const uint32_t w0 = lds32(a), w1 = lds32(a + 4), w2 = lds32(a + 8);
+    lo = __funnelshift_r(w0, w1, sh);
+    hi = __funnelshift_r(w1, w2, sh);
+  }
+  __device__ __forceinline__ static uint32_t assemble(uint32_t ql, uint32_t qh, int s) {
+    const uint32_t lo = (s >= 2 ? (ql >> 4) : ql) & 0x0F0F0F0Fu;
+    const uint32_t hb = (s == 0 ? (qh << 4) : s == 1 ? (qh << 2) : s == 2 ? qh : (qh >> 2)) & 0x30303030u;
+    return lo | hb | 0x80808080u;
+  }
+  __device__ __forceinline__ static void run(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg, bool ftz,
+                                             float (&acc)[4], uint32_t sh) {
+    const float da = fp16_bits_to_f32(lds_u16(ra + 208), ftz);
+    const float db = fp16_bits_to_f32(lds_u16(rb + 208), ftz);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint64_t Da[4], Ca[4], Db[4], Cb[4];
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const int si = 192 + 8 * h + 2 * s + (c >> 1);
+        const float dsa = da * static_cast<float>(static_cast<int8_t>(ra[si]));
+        const float dsb = db * static_cast<float>(static_cast<int8_t>(rb[si]));
+        Da[s] = dup2(dsa * 128.0f);
+        Ca[s] = dup2(dsa * -160.0f);
+        Db[s] = dup2(dsb * 128.0f);
+        Cb[s] = dup2(dsb * -160.0f);
+      }
+      uint32_t qla[2], qlb[2], qha[2], qla_b[2], qlb_b[2], qh_b[2];
+      load8(ra + 64 * h + 8 * c, sh, qla[0], qla[1]);
+      load8(ra + 64 * h + 32 + 8 * c, sh, qlb[0], qlb[1]);
+      load8(ra + 128 + 32 * h + 8 * c, sh, qha[0], qha[1]);
+      load8(rb + 64 * h + 8 * c, sh, qla_b[0], qla_b[1]);
+      load8(rb + 64 * h + 32 + 8 * c, sh, qlb_b[0], qlb_b[1]);
+      load8(rb + 128 + 32 * h + 8 * c, sh, qh_b[0], qh_b[1]);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const uint32_t qa = assemble((s & 1) ? qlb[half] : qla[half], qha[half], s);
+          const uint32_t qb = assemble((s & 1) ? qlb_b[half] : qla_b[half], qh_b[half], s);
+          const uint2 b = *reinterpret_cast<const uint2*>(xg + 32 * (8 * h + 4 * half + s));
+          mma_bf16_16816(acc, fma2_pack(byte_to_f2<0>(qa), byte_to_f2<1>(qa), Da[s], Ca[s]),
+                         fma2_pack(byte_to_f2<0>(qb), byte_to_f2<1>(qb), Db[s], Cb[s]),
+                         fma2_pack(byte_to_f2<2>(qa), byte_to_f2<3>(qa), Da[s], Ca[s]),
+                         fma2_pack(byte_to_f2<2>(qb), byte_to_f2<3>(qb), Db[s], Cb[s]), b.x, b.y);
+        }
+      }
+    }
+  }
+  __host__ __device__ __forceinline__ static int xk(int t, int c) {
+    const int h = t >> 3, half = (t >> 2) & 1, s = t & 3;
+    return 128 * h + 32 * s + 8 * c + 4 * half;
+  }
+};
+
+}  // namespace spiral

@@ -1,0 +1,530 @@
+// moe.cu — MoE FFN decode layer with quantized experts:
+// for every token t and each of its top-k routed experts e_{t,j} with weight
+// w_{t,j}:
+//   h_{t,j} = bf16( silu(x_t Wg_e^T) * (x_t Wu_e^T) )          [I]
+//   y_t     = sum_j w_{t,j} * (h_{t,j} Wd_e^T)                  [H]
+// with gate/up [I rows x H] and down [H rows x I] canonical GGUF tensors per
+// expert, fp32 accumulation everywhere and one bf16 rounding of h (the down
+// projection consumes bf16 activations) and of y.
+//
+// Only experts in the local range [e0, e0 + E_local) contribute; others are
+// skipped, so expert-parallel ranks each compute their share and the caller
+// combines across ranks.
+//
+// Four stream-ordered kernels, each launched with programmatic stream
+// serialization (every kernel waits for its predecessor before it reads
+// anything that predecessor wrote):
+//   1. moe_route   one CTA: bucket the (token, slot) pairs of local experts by
+//                  expert (counting sort) and cut each expert's pairs into
+//                  problems of at most 8 (the MMA N width).
+//   2. moe_gemv<1> gate+up: work item = (problem, 16 intermediate features);
+//                  a stage holds the 16 gate rows and the 16 up rows; the
+//                  epilogue applies SwiGLU and stores h in bf16.
+//   3. moe_gemv<2> down: work item = (problem, 16 output features); the
+//                  epilogue stores w_{t,j} * y_e in fp32 per pair.
+//   4. moe_combine y_t = sum over slots j in order (deterministic).
+// The grouped GEMVs reuse the decode GEMV's machinery (gemv_decode.cuh): one
+// persistent CTA per SM, a producer warp streaming whole weight rows with 1-D
+// bulk copies, two groups of 8 consumer warps on mma.sync.  Work items are
+// cut into one contiguous range per CTA; each group restages its activation
+// rows only when its next item belongs to a different problem.
+//
+// Scratch (counts, pair lists, problem table, h, per-pair outputs) lives in a
+// caller-provided workspace (spiral_moe_workspace_bytes).
+#include <atomic>
+
+#include "api_internal.h"
+#include "gemv_decode.cuh"
+
+namespace spiral {
+
+namespace {
+
+constexpr int kMoeGroups = 2;
+constexpr int kMoeWarpsPerGroup = 8;
+constexpr int kMoeGroupThreads = kMoeWarpsPerGroup * 32;
+constexpr int kMoeConsumers = kMoeGroups * kMoeWarpsPerGroup;
+constexpr int kMoeThreads = (kMoeConsumers + 1) * 32;
+constexpr int kMoeMaxStages = 8;
+constexpr int kMoeBarrierBytes = 256;
+constexpr int kRouteThreads = 1024;
+constexpr int kTileRows = 16;
+
+struct MoeProblem {
+  int expert;  // local expert index
+  int first;   // offset into the sorted pair list
+  int nx;      // pairs (activation rows), 1..8
+  int pad;
+};
+
+struct MoeLayout {
+  // all offsets in bytes from the workspace base, 256-byte aligned
+  size_t hdr, cnt, start, cursor, pairs, problems, h, part, total;
+  int64_t max_pairs, max_problems;
+};
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+MoeLayout moe_layout(int64_t E_local, int64_t H, int64_t I, int64_t T, int64_t topk) {
+  MoeLayout L{};
+  L.max_pairs = T * topk;
+  L.max_problems = L.max_pairs / 8 + E_local + 1;
+  size_t off = 0;
+  L.hdr = off;
+  off = align256(off + 4 * sizeof(int));
+  L.cnt = off;
+  off = align256(off + E_local * sizeof(int));
+  L.start = off;
+  off = align256(off + E_local * sizeof(int));
+  L.cursor = off;
+  off = align256(off + E_local * sizeof(int));
+  L.pairs = off;
+  off = align256(off + L.max_pairs * sizeof(int));
+  L.problems = off;
+  off = align256(off + L.max_problems * sizeof(MoeProblem));
+  L.h = off;
+  off = align256(off + L.max_pairs * I * 2);
+  L.part = off;
+  off = align256(off + L.max_pairs * H * sizeof(float));
+  L.total = off;
+  return L;
+}
+
+struct MoeArgs {
+  int fmt;
+  const uint8_t* w_gate;  // [E_local][I][row_bytes(H)]
+  const uint8_t* w_up;
+  const uint8_t* w_down;  // [E_local][H][row_bytes(I)]
+  int64_t rb_h, rb_i;     // row bytes of a gate/up row (K = H) and a down row (K = I)
+  const uint16_t* x;      // [T][x_stride] bf16
+  int64_t x_stride;
+  const int32_t* ids;     // [T][topk] global expert ids
+  const float* wts;       // [T][topk]
+  void* y;                // [T][y_stride]
+  int64_t y_stride;
+  int y_bf16, accumulate, ftz;
+  int T, topk, H, I, e0, E_local;
+  uint8_t* ws;
+  MoeLayout L;
+};
+
+// ------------------------------------------------------------- routing ----
+
+__global__ void __launch_bounds__(kRouteThreads) moe_route(const MoeArgs a) {
+  extern __shared__ int sh[];
+  int* scnt = sh;
+  int* sstart = sh + a.E_local;
+  int* scur = sh + 2 * a.E_local;
+  griddep_launch_dependents();
+  griddep_wait();
+  int* hdr = reinterpret_cast<int*>(a.ws + a.L.hdr);
+  int* pairs = reinterpret_cast<int*>(a.ws + a.L.pairs);
+  MoeProblem* probs = reinterpret_cast<MoeProblem*>(a.ws + a.L.problems);
+  const int np_total = a.T * a.topk;
+  for (int e = threadIdx.x; e < a.E_local; e += blockDim.x) {
+    scnt[e] = 0;
+    scur[e] = 0;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < np_total; i += blockDim.x) {
+    const int e = a.ids[i] - a.e0;
+    if (e >= 0 && e < a.E_local) atomicAdd(&scnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0, np = 0;
+    for (int e = 0; e < a.E_local; ++e) {
+      sstart[e] = run;
+      for (int c = 0; c < scnt[e]; c += 8) {
+        MoeProblem pr;
+        pr.expert = e;
+        pr.first = run + c;
+        pr.nx = min(8, scnt[e] - c);
+        pr.pad = 0;
+        probs[np++] = pr;
+      }
+      run += scnt[e];
+    }
+    hdr[0] = np;
+    hdr[1] = run;
+  }
+  __syncthreads();
+  // Order inside an expert's list does not change any result: each pair is
+  // its own MMA column, computed with the same summation order.
+  for (int i = threadIdx.x; i < np_total; i += blockDim.x) {
+    const int e = a.ids[i] - a.e0;
+    if (e >= 0 && e < a.E_local) pairs[sstart[e] + atomicAdd(&scur[e], 1)] = i;
+  }
+}
+
+// ------------------------------------------------------- grouped GEMV -----
+
+template <int PHASE>
+struct MoePhase;
+template <>
+struct MoePhase<1> {  // gate + up, K = H, 16 intermediate features per item
+  static constexpr int kRows = 32;
+};
+template <>
+struct MoePhase<2> {  // down, K = I, 16 output features per item
+  static constexpr int kRows = 16;
+};
+
+// Stage the activation rows of one problem for one consumer group in the
+// permuted fragment order of gemv_decode.cuh: row m (< nx) comes from
+// src(m).  Four rows at a time, each thread first loads its 16-byte pieces of
+// those rows (one L2 round trip), then each row goes through `raw` and is
+// permuted.
+template <int FMT, typename Src>
+__device__ void moe_stage_rows(int nx, int K, Src src, uint8_t* xs, int x_pitch, uint8_t* raw, int gt, int bar_id) {
+  using F = GemvFmt<FMT>;
+  constexpr int kStepShift = F::kSteps == 8 ? 3 : 4;
+  constexpr int kMaxPieces = 2;  // K <= 2 * 8 * 256 = 4096
+  constexpr int kRowsPerRound = 4;
+  const int pieces = K / 8;
+  const int per_m = (K / F::kGroupK) * F::kSteps * 4;
+  for (int m0 = 0; m0 < nx; m0 += kRowsPerRound) {
+    uint4 v[kRowsPerRound][kMaxPieces];
+#pragma unroll
+    for (int mm = 0; mm < kRowsPerRound; ++mm) {
+#pragma unroll
+      for (int i = 0; i < kMaxPieces; ++i) {
+        const int q = gt + i * kMoeGroupThreads;
+        if (m0 + mm < nx && q < pieces) v[mm][i] = __ldg(reinterpret_cast<const uint4*>(src(m0 + mm)) + q);
+      }
+    }
+#pragma unroll
+    for (int mm = 0; mm < kRowsPerRound; ++mm) {
+      const int m = m0 + mm;
+      if (m < nx) {
+#pragma unroll
+        for (int i = 0; i < kMaxPieces; ++i) {
+          const int q = gt + i * kMoeGroupThreads;
+          if (q < pieces) reinterpret_cast<uint4*>(raw)[q] = v[mm][i];
+        }
+        named_bar_sync(bar_id, kMoeGroupThreads);
+        const uint16_t* xr = reinterpret_cast<const uint16_t*>(raw);
+        uint8_t* dst = xs + m * x_pitch;
+        for (int e = gt; e < per_m; e += kMoeGroupThreads) {
+          const int c = e & 3, gs = e >> 2, st = gs & (F::kSteps - 1), g = gs >> kStepShift;
+          const int k = g * F::kGroupK + GroupDecoder<FMT>::xk(st, c);
+          *reinterpret_cast<uint2*>(dst + gs * 32 + c * 8) =
+              make_uint2(xr[k] | (static_cast<uint32_t>(xr[k + 1]) << 16),
+                         xr[k + 2] | (static_cast<uint32_t>(xr[k + 3]) << 16));
+        }
+        named_bar_sync(bar_id, kMoeGroupThreads);
+      }
+    }
+  }
+}
+
+template <int FMT>
+__device__ __forceinline__ void moe_decode_group(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg,
+                                                 bool ftz, float (&acc)[4], int gl) {
+  if constexpr (FMT == kQ6_K) {
+    GroupDecoder<FMT>::run(ra, rb, c, xg, ftz, acc, (gl & 1) ? 16u : 0u);
+  } else {
+    GroupDecoder<FMT>::run(ra, rb, c, xg, ftz, acc);
+  }
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+
+template <int FMT, int PHASE>
+__global__ void __launch_bounds__(kMoeThreads, 1) moe_gemv(const MoeArgs a, int stages, int row_pitch, int x_pitch) {
+  using F = GemvFmt<FMT>;
+  using P = MoePhase<PHASE>;
+  constexpr int kAcc = PHASE == 1 ? 2 : 1;
+  const int K = PHASE == 1 ? a.H : a.I;
+  const int N = PHASE == 1 ? a.I : a.H;
+  const int64_t rb = PHASE == 1 ? a.rb_h : a.rb_i;
+  const int tiles = N / kTileRows;
+  const int groups_per_row = K / F::kGroupK;
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kMoeMaxStages;
+  int& abort_flag = *reinterpret_cast<int*>(smem + kMoeBarrierBytes - 8);
+  float4* red = reinterpret_cast<float4*>(smem + kMoeBarrierBytes);  // [groups][kAcc][8 warps][32]
+  uint8_t* xbuf = smem + kMoeBarrierBytes + kMoeConsumers * 32 * 16 * kAcc;  // [groups][8][x_pitch]
+  uint8_t* stg = xbuf + kMoeGroups * 8 * x_pitch;
+  const int stage_bytes = P::kRows * row_pitch;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kMoeWarpsPerGroup);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+    griddep_launch_dependents();
+  }
+  __syncthreads();
+  griddep_wait();  // the route kernel (and for phase 2 the gate/up kernel) wrote what follows
+
+  const int* hdr = reinterpret_cast<const int*>(a.ws + a.L.hdr);
+  const int* pairs = reinterpret_cast<const int*>(a.ws + a.L.pairs);
+  const MoeProblem* probs = reinterpret_cast<const MoeProblem*>(a.ws + a.L.problems);
+  const int64_t items = static_cast<int64_t>(hdr[0]) * tiles;
+  const int64_t i_begin = blockIdx.x * items / gridDim.x, i_end = (blockIdx.x + 1) * items / gridDim.x;
+
+  if (warp == kMoeConsumers) {
+    // ------------------------------------------------------- producer ----
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      const uint32_t bytes = static_cast<uint32_t>(rb);
+      uint32_t it = 0;
+      for (int64_t i = i_begin; i < i_end; ++i, ++it) {
+        const MoeProblem pr = probs[i / tiles];
+        const int tile = static_cast<int>(i % tiles);
+        const int s = static_cast<int>(it % stages);
+        if (!mbar_wait(&empty[s], ((it / stages) & 1u) ^ 1u) || *(volatile int*)&abort_flag) {
+          abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], bytes * P::kRows);
+        uint8_t* dst = stg + s * stage_bytes;
+        const int64_t row0 = static_cast<int64_t>(pr.expert) * N + tile * kTileRows;
+        if constexpr (PHASE == 1) {
+          for (int r = 0; r < kTileRows; ++r) {
+            bulk_g2s(dst + r * row_pitch, a.w_gate + (row0 + r) * rb, bytes, &full[s], pol);
+            bulk_g2s(dst + (kTileRows + r) * row_pitch, a.w_up + (row0 + r) * rb, bytes, &full[s], pol);
+          }
+        } else {
+          for (int r = 0; r < kTileRows; ++r)
+            bulk_g2s(dst + r * row_pitch, a.w_down + (row0 + r) * rb, bytes, &full[s], pol);
+        }
+      }
+      // Every issued stage must land before the CTA may exit.
+      const uint32_t first = it > static_cast<uint32_t>(stages) ? it - stages : 0u;
+      for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % stages], (j / stages) & 1u);
+    }
+    return;
+  }
+
+  // --------------------------------------------------------- consumers -----
+  const int grp = warp / kMoeWarpsPerGroup, gw = warp % kMoeWarpsPerGroup;
+  const int gt = gw * 32 + lane;
+  const int r = lane >> 2, c = lane & 3;
+  const bool ftz = a.ftz != 0;
+  float4* gred = red + grp * (kAcc * kMoeWarpsPerGroup * 32);
+  uint8_t* xs = xbuf + grp * 8 * x_pitch;
+  const int bar_id = 1 + grp;
+  int staged = -1;  // problem whose rows are in xs
+  uint32_t it = 0;
+  for (int64_t i = i_begin; i < i_end; ++i, ++it) {
+    if (static_cast<int>((i - i_begin) % kMoeGroups) != grp) continue;
+    const int pidx = static_cast<int>(i / tiles);
+    const int tile = static_cast<int>(i % tiles);
+    const MoeProblem pr = probs[pidx];
+    if (pidx != staged) {
+      if constexpr (PHASE == 1) {
+        auto src = [&](int m) { return a.x + static_cast<int64_t>(pairs[pr.first + m] / a.topk) * a.x_stride; };
+        moe_stage_rows<FMT>(pr.nx, K, src, xs, x_pitch, reinterpret_cast<uint8_t*>(gred), gt, bar_id);
+      } else {
+        const uint16_t* h = reinterpret_cast<const uint16_t*>(a.ws + a.L.h);
+        auto src = [&](int m) { return h + static_cast<int64_t>(pairs[pr.first + m]) * a.I; };
+        moe_stage_rows<FMT>(pr.nx, K, src, xs, x_pitch, reinterpret_cast<uint8_t*>(gred), gt, bar_id);
+      }
+      staged = pidx;
+    }
+    const int mx = r < pr.nx ? r : 0;  // columns >= nx read row 0 and are discarded
+    const uint8_t* xcol = xs + mx * x_pitch + c * 8;
+    const int s = static_cast<int>(it % stages);
+    float acc[kAcc][4] = {};
+    bool ready = false;
+    if (!*(volatile int*)&abort_flag) {
+      ready = mbar_wait(&full[s], (it / stages) & 1u);
+      if (!ready) abort_flag = 1;
+    }
+    if (ready) {
+      const uint8_t* st = stg + s * stage_bytes;
+      for (int gl = gw; gl < groups_per_row; gl += kMoeWarpsPerGroup) {
+        const uint8_t* xg = xcol + gl * (F::kSteps * 32);
+#pragma unroll
+        for (int ac = 0; ac < kAcc; ++ac) {
+          const uint8_t* base = st + ac * kTileRows * row_pitch + gl * F::kGroupBytes;
+          moe_decode_group<FMT>(base + r * row_pitch, base + (r + 8) * row_pitch, c, xg, ftz, acc[ac], gl);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+    for (int ac = 0; ac < kAcc; ++ac)
+      gred[(ac * kMoeWarpsPerGroup + gw) * 32 + lane] = make_float4(acc[ac][0], acc[ac][1], acc[ac][2], acc[ac][3]);
+    named_bar_sync(bar_id, kMoeGroupThreads);
+    if (gw < 4) {
+      const int l = gt >> 2, j = gt & 3;
+      float v[kAcc];
+#pragma unroll
+      for (int ac = 0; ac < kAcc; ++ac) {
+        v[ac] = 0.f;
+#pragma unroll
+        for (int w = 0; w < kMoeWarpsPerGroup; ++w)
+          v[ac] += reinterpret_cast<const float*>(&gred[(ac * kMoeWarpsPerGroup + w) * 32 + l])[j];
+      }
+      const int row = (l >> 2) + 8 * (j >> 1);
+      const int m = 2 * (l & 3) + (j & 1);
+      if (ready && m < pr.nx) {
+        const int pair = pairs[pr.first + m];
+        const int feat = tile * kTileRows + row;
+        if constexpr (PHASE == 1) {
+          uint16_t* h = reinterpret_cast<uint16_t*>(a.ws + a.L.h);
+          h[static_cast<int64_t>(pair) * a.I + feat] =
+              static_cast<uint16_t>(pack_bf16x2(silu(v[0]) * v[kAcc - 1], 0.f) & 0xFFFFu);
+        } else {
+          float* part = reinterpret_cast<float*>(a.ws + a.L.part);
+          part[static_cast<int64_t>(pair) * a.H + feat] = a.wts[pair] * v[0];
+        }
+      }
+    }
+    named_bar_sync(bar_id, kMoeGroupThreads);  // gred is free again
+  }
+}
+
+// y[t][n] = sum over local slots j (in order) of part[t*topk + j][n].
+__global__ void moe_combine(const MoeArgs a) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const float* part = reinterpret_cast<const float*>(a.ws + a.L.part);
+  const int64_t total = static_cast<int64_t>(a.T) * a.H;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(e / a.H), n = static_cast<int>(e % a.H);
+    float sum = 0.f;
+    for (int j = 0; j < a.topk; ++j) {
+      const int pair = t * a.topk + j;
+      const int ex = a.ids[pair] - a.e0;
+      if (ex >= 0 && ex < a.E_local) sum += part[static_cast<int64_t>(pair) * a.H + n];
+    }
+    const int64_t off = static_cast<int64_t>(t) * a.y_stride + n;
+    if (a.y_bf16) {
+      static_cast<uint16_t*>(a.y)[off] = static_cast<uint16_t>(pack_bf16x2(sum, 0.f) & 0xFFFFu);
+    } else if (a.accumulate) {
+      static_cast<float*>(a.y)[off] += sum;
+    } else {
+      static_cast<float*>(a.y)[off] = sum;
+    }
+  }
+}
+
+cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, void** args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+template <int FMT, int PHASE>
+cudaError_t launch_moe_gemv(const MoeArgs& a, cudaStream_t stream) {
+  using F = GemvFmt<FMT>;
+  constexpr int kAcc = PHASE == 1 ? 2 : 1;
+  const int K = PHASE == 1 ? a.H : a.I;
+  const int64_t rb = PHASE == 1 ? a.rb_h : a.rb_i;
+  const int rows = MoePhase<PHASE>::kRows;
+  const int x_pitch = K * 2 + 32;
+  const int row_pitch = static_cast<int>(rb) + 16;
+  const size_t fixed = kMoeBarrierBytes + size_t(kMoeConsumers) * 32 * 16 * kAcc + size_t(kMoeGroups) * 8 * x_pitch;
+  const size_t avail = device_max_smem_optin();
+  if (fixed + size_t(2) * rows * row_pitch > avail) return cudaErrorInvalidValue;
+  const int stages = static_cast<int>(std::min<size_t>(kMoeMaxStages, (avail - fixed) / (size_t(rows) * row_pitch)));
+  const size_t smem = fixed + size_t(stages) * rows * row_pitch;
+  (void)F::kGroupK;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::atomic<bool> configured[64];
+  if (!configured[dev & 63].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(moe_gemv<FMT, PHASE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(avail));
+    if (e != cudaSuccess) return e;
+    configured[dev & 63].store(true, std::memory_order_release);
+  }
+  MoeArgs args = a;
+  int st = stages, rp = row_pitch, xp = x_pitch;
+  void* kargs[] = {&args, &st, &rp, &xp};
+  return launch_pdl(reinterpret_cast<const void*>(moe_gemv<FMT, PHASE>), dim3(device_sm_count()), dim3(kMoeThreads),
+                    smem, stream, kargs);
+}
+
+template <int FMT>
+cudaError_t moe_run(const MoeArgs& a, cudaStream_t stream) {
+  MoeArgs args = a;
+  {
+    void* kargs[] = {&args};
+    const size_t smem = size_t(3) * a.E_local * sizeof(int);
+    cudaError_t e = launch_pdl(reinterpret_cast<const void*>(moe_route), dim3(1), dim3(kRouteThreads), smem, stream,
+                               kargs);
+    if (e != cudaSuccess) return e;
+  }
+  cudaError_t e = launch_moe_gemv<FMT, 1>(a, stream);
+  if (e != cudaSuccess) return e;
+  e = launch_moe_gemv<FMT, 2>(a, stream);
+  if (e != cudaSuccess) return e;
+  const int64_t total = static_cast<int64_t>(a.T) * a.H;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, int64_t(device_sm_count()) * 8));
+  void* kargs[] = {&args};
+  return launch_pdl(reinterpret_cast<const void*>(moe_combine), dim3(blocks), dim3(256), 0, stream, kargs);
+}
+
+}  // namespace
+
+size_t moe_workspace_bytes(int64_t E_local, int64_t H, int64_t I, int64_t T, int64_t topk) {
+  return moe_layout(E_local, H, I, T, topk).total;
+}
+
+bool moe_shape_ok(int fmt, int64_t H, int64_t I) {
+  // weight rows a whole number of 16-byte runs (bulk copies) and of decode
+  // groups; an activation row fits the group's staging buffer (H <= 4096,
+  // I <= 2048)
+  const int64_t unit = fmt == kQ6_K ? 2048 : 256;
+  if (H % unit != 0 || I % unit != 0) return false;
+  return H <= 4096 && I <= 2048;
+}
+
+cudaError_t moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w_down, const void* x,
+                    int64_t x_stride, const int32_t* ids, const float* wts, void* y, int64_t y_stride, bool y_bf16,
+                    bool accumulate, bool ftz, int64_t T, int64_t topk, int64_t H, int64_t I, int64_t e0,
+                    int64_t E_local, void* ws, cudaStream_t stream) {
+  MoeArgs a{};
+  a.fmt = fmt;
+  a.w_gate = static_cast<const uint8_t*>(w_gate);
+  a.w_up = static_cast<const uint8_t*>(w_up);
+  a.w_down = static_cast<const uint8_t*>(w_down);
+  const int64_t bk = fmt == kQ6_K ? 256 : 32, bb = fmt == kQ4_0 ? 18 : (fmt == kQ8_0 ? 34 : 210);
+  a.rb_h = H / bk * bb;
+  a.rb_i = I / bk * bb;
+  a.x = static_cast<const uint16_t*>(x);
+  a.x_stride = x_stride;
+  a.ids = ids;
+  a.wts = wts;
+  a.y = y;
+  a.y_stride = y_stride;
+  a.y_bf16 = y_bf16;
+  a.accumulate = accumulate;
+  a.ftz = ftz;
+  a.T = static_cast<int>(T);
+  a.topk = static_cast<int>(topk);
+  a.H = static_cast<int>(H);
+  a.I = static_cast<int>(I);
+  a.e0 = static_cast<int>(e0);
+  a.E_local = static_cast<int>(E_local);
+  a.ws = static_cast<uint8_t*>(ws);
+  a.L = moe_layout(E_local, H, I, T, topk);
+  switch (fmt) {
+    case kQ4_0: return moe_run<kQ4_0>(a, stream);
+    case kQ8_0: return moe_run<kQ8_0>(a, stream);
+    case kQ6_K: return moe_run<kQ6_K>(a, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace spiral

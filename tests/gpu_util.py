@@ -37,8 +37,8 @@ def strided_rows(raw: np.ndarray, N: int, row_bytes: int, stride: int) -> np.nda
     return out
 
 
-def tolerance_ok(y: np.ndarray, ref: np.ndarray, bf16_out: bool):
-    """The stated MUL_MAT tolerance:
+def tolerance_ok(y: np.ndarray, ref: np.ndarray, bf16_out: bool, rel_tol: float = 1e-3):
+    """The stated MUL_MAT tolerance (rel_tol = 1e-3):
          |y - ref| <= 1e-3 * |ref| + 1e-3 * rms(ref)      (fp32 output)
        plus one bf16 rounding, 2^-8 * |ref|, for bf16 output.
     ref is the float64 dequant-then-matmul oracle.  Mirrors the reference's
@@ -47,7 +47,7 @@ def tolerance_ok(y: np.ndarray, ref: np.ndarray, bf16_out: bool):
     ref = np.asarray(ref, dtype=np.float64)
     err = np.abs(np.asarray(y, dtype=np.float64) - ref)
     rms = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
-    tol = 1e-3 * np.abs(ref) + 1e-3 * rms
+    tol = rel_tol * np.abs(ref) + rel_tol * rms
     if bf16_out:
         tol = tol + 2.0**-8 * np.abs(ref)
     ok = bool(np.all(err <= tol))

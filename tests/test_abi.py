@@ -138,3 +138,28 @@ def test_python_mirror_raises_on_error():
     with pytest.raises(sp.SpiralError) as e:
         sp._check(sp.lib().spiral_dequant_bf16(sp.Q4_0, 0, 18, 16, 32, 32, 1, 0, 0))
     assert e.value.status == -3
+
+
+def test_moe_validation_codes():
+    L = sp.lib()
+    assert sp.moe_workspace_bytes(128, 2048, 768, 64, 8) > 64 * 8 * 2048 * 4
+    assert sp.moe_workspace_bytes(0, 2048, 768, 64, 8) == 0
+
+    def call(**kw):
+        a = dict(fmt=sp.Q4_0, wg=256, wu=256, wd=256, E=8, e0=0, H=2048, I=768, x=256, xs=2048, T=4, ids=256,
+                 w=256, topk=8, y=256, yd=sp.BF16, ys=2048, ws=256, wsb=1 << 30, flags=0)
+        a.update(kw)
+        return L.spiral_moe_ffn(a["fmt"], a["wg"], a["wu"], a["wd"], a["E"], a["e0"], a["H"], a["I"], a["x"],
+                                a["xs"], a["T"], a["ids"], a["w"], a["topk"], a["y"], a["yd"], a["ys"], a["ws"],
+                                a["wsb"], a["flags"], 0)
+
+    assert call(fmt=5) == -1
+    assert call(H=2000) == -2  # not a multiple of 256
+    assert call(I=4096) == -2  # above the staging limit
+    assert call(T=0) == -2
+    assert call(wg=0) == -3
+    assert call(x=264) == -4  # activations must be 16-byte aligned
+    assert call(xs=2052) == -4
+    assert call(ws=260) == -4
+    assert call(wsb=1024) == -5  # workspace too small
+    assert call(yd=7) == -10

@@ -128,3 +128,28 @@ def test_q6_k_encoder_roundtrip():
     vals = F.dequant_f32(F.Q6_K, raw, 256, 5)
     expect = (q6.astype(np.int32) - 32) * np.repeat(sc.astype(np.int32), 16, axis=1)
     assert np.array_equal(vals, expect.astype(np.float32))
+
+
+def test_moe_oracle_matches_a_plain_loop():
+    """oracle.moe_ffn_f64 (C dequant, per-expert batching) against a per-slot
+    loop over the NumPy restatement."""
+    fid, E, H, I, T, topk = F.Q4_0, 6, 64, 32, 5, 3
+    wg = F.gen_experts(fid, E, I, H, seed=1)
+    wu = F.gen_experts(fid, E, I, H, seed=2)
+    wd = F.gen_experts(fid, E, H, I, seed=3)
+    x = F.gen_activations(T, H, seed=4)
+    ids, w = F.gen_routing(T, E, topk, seed=5)
+    got = oracle.moe_ffn_f64(fid, wg, wu, wd, x, ids, w, H, I, E)
+    gu, dd = I * F.row_bytes(fid, H), H * F.row_bytes(fid, I)
+    xf = F.bf16_bits_to_f32(x).astype(np.float64)
+    want = np.zeros((T, H))
+    for t in range(T):
+        for j in range(topk):
+            e = int(ids[t, j])
+            Wg = F.bf16_bits_to_f32(F.dequant_bf16(fid, wg[e * gu:(e + 1) * gu], H, I)).astype(np.float64)
+            Wu = F.bf16_bits_to_f32(F.dequant_bf16(fid, wu[e * gu:(e + 1) * gu], H, I)).astype(np.float64)
+            Wd = F.bf16_bits_to_f32(F.dequant_bf16(fid, wd[e * dd:(e + 1) * dd], I, H)).astype(np.float64)
+            g, u = Wg @ xf[t], Wu @ xf[t]
+            h = (g / (1 + np.exp(-g)) * u).astype(np.float32).astype(bfloat16).astype(np.float64)
+            want[t] += float(w[t, j]) * (Wd @ h)
+    np.testing.assert_allclose(got, want, rtol=1e-12, atol=1e-12)
