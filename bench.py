@@ -280,11 +280,14 @@ def run_spiral(args):
 
     fid = F.BY_NAME[args.fmt]
     K, N = K_DIM, N_DIM
-    assert N % (8 * world) == 0
-    Nr = N // world
+    from spiral_b200.dist import gather_rows, row_range
+
+    n0, n1 = row_range(N, world, rank)
+    Nr = n1 - n0
+    assert Nr * world == N, "equal row shards (N a multiple of 16 * world)"
     rb = F.row_bytes(fid, K)
     raw = F.generate(fid, K, N, seed=0)
-    shard = raw[rank * Nr * rb : (rank + 1) * Nr * rb]
+    shard = raw[n0 * rb : n1 * rb]
     shard_bytes = Nr * rb
     copies = max(2, min(256, math.ceil(2 * L2_BYTES / shard_bytes)))
     w0 = torch.from_numpy(shard).to(dev)
@@ -292,7 +295,7 @@ def run_spiral(args):
     xs = {B: torch.from_numpy(F.gen_activations(B, K, seed=100 + B).view(np.int16)).to(dev).view(torch.bfloat16)
           for B in BATCHES}
     ys = {B: torch.empty((B, Nr), dtype=torch.bfloat16, device=dev) for B in BATCHES}
-    yg = {B: torch.empty((world, B, Nr), dtype=torch.bfloat16, device=dev) for B in BATCHES} if world > 1 else None
+    yfull = {}
 
     # every MUL_MAT of the sweep reads a different weight copy, so no launch
     # finds its weights in L2 (the last use of a copy is `copies` launches ago)
@@ -303,7 +306,7 @@ def run_spiral(args):
             yb = ys[B] if y is None else y[B]
             sp.mul_mat(fid, w, xb, Nr, K, yb, y_dtype=sp.BF16, static_weights=True)
             if world > 1:
-                dist.all_gather_into_tensor(yg[B], yb)
+                yfull[B] = gather_rows(yb, N)
 
     stream = torch.cuda.Stream(device=dev)
     # warm-up (also configures kernel attributes and the per-stream GEMV
@@ -397,8 +400,7 @@ def run_spiral(args):
             xd[B].view(torch.int16).copy_(hx[B], non_blocking=True)
             sp.mul_mat(fid, w, xd[B], Nr, K, ys[B], y_dtype=sp.BF16, static_weights=True)
             if world > 1:
-                dist.all_gather_into_tensor(yg[B], ys[B])
-                hy[B].view(B, N).copy_(yg[B].permute(1, 0, 2).reshape(B, N).view(torch.int16), non_blocking=True)
+                hy[B].view(B, N).copy_(gather_rows(ys[B], N).view(torch.int16), non_blocking=True)
             else:
                 hy[B].copy_(ys[B].view(torch.int16), non_blocking=True)
 
@@ -459,6 +461,51 @@ def run_spiral(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+MOE_BYTES_PER_EXPERT = 2654208  # Q4_0 gate + up (768 x 2048) and down (2048 x 768)
+
+
+def bench_moe(sp, F, dev, timed, graph_steps, hbm_peak, Ts=(1, 2, 4, 8, 16, 32, 64)):
+    """Config 4: MoE FFN decode layer, 128 Q4_0 experts (hidden 2048, inter
+    768, SwiGLU), top-8, T tokens.  Weight GB/s = unique active experts x
+    2,654,208 B per layer / time.  8 copies of the expert weights and 8
+    routings rotate, so a layer's experts were last touched >= 8 layers ago
+    (>= 168 MB of other weights: not in L2)."""
+    import torch
+
+    fid, E, H, I, topk, copies, routings = F.Q4_0, 128, 2048, 768, 8, 8, 8
+    g0 = torch.from_numpy(F.gen_experts(fid, E, I, H, seed=11)).to(dev)
+    u0 = torch.from_numpy(F.gen_experts(fid, E, I, H, seed=12)).to(dev)
+    d0 = torch.from_numpy(F.gen_experts(fid, E, H, I, seed=13)).to(dev)
+    wg = [g0] + [g0.clone() for _ in range(copies - 1)]
+    wu = [u0] + [u0.clone() for _ in range(copies - 1)]
+    wd = [d0] + [d0.clone() for _ in range(copies - 1)]
+    res = {}
+    for T in Ts:
+        x = torch.from_numpy(F.gen_activations(T, H, seed=T).view(np.int16)).to(dev).view(torch.bfloat16)
+        rts = [F.gen_routing(T, E, topk, seed=1000 * T + r) for r in range(routings)]
+        uniq = [len(set(ids.reshape(-1).tolist())) for ids, _ in rts]
+        ids = [torch.from_numpy(a).to(dev) for a, _ in rts]
+        wts = [torch.from_numpy(b).to(dev) for _, b in rts]
+        y = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        ws = torch.empty(sp.moe_workspace_bytes(E, H, I, T, topk), dtype=torch.uint8, device=dev)
+
+        def body(i, x=x, ids=ids, wts=wts, y=y, ws=ws):
+            c, r = i % copies, (i // copies) % routings
+            sp.moe_ffn(fid, wg[c], wu[c], wd[c], x, ids[r], wts[r], hidden=H, inter=I, n_experts_local=E, y=y,
+                       workspace=ws)
+
+        steps = graph_steps * 4
+        ms = timed(steps, 3, body, {})
+        t = ms / steps * 1e-3
+        # the captured graph cycles over graph_steps calls: average U over those
+        u_mean = sum(uniq[(i // copies) % routings] for i in range(graph_steps)) / graph_steps
+        wbytes = u_mean * MOE_BYTES_PER_EXPERT
+        res[f"T{T}"] = {"us": t * 1e6, "unique_experts": u_mean, "weight_GBps": wbytes / t / 1e9,
+                        "frac_hbm": (wbytes + T * H * 4) / t / 1e9 / hbm_peak}
+    del wg, wu, wd
+    return res
 
 
 def bench_extras(sp, F, dev, K, N, timed, graph_steps, hbm_peak):
@@ -525,6 +572,7 @@ def bench_extras(sp, F, dev, K, N, timed, graph_steps, hbm_peak):
         out["dequant"][f"{name}_{Nd}x{K}"] = {"us": t * 1e6, "GBps": (in_b + out_b) / t / 1e9,
                                               "frac_hbm": (in_b + out_b) / t / 1e9 / hbm_peak}
         del srcs, dsts
+    out["moe"] = bench_moe(sp, F, dev, timed, graph_steps, hbm_peak)
     return out
 
 
