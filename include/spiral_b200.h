@@ -241,6 +241,29 @@ SPIRAL_API int spiral_moe_ffn(int fmt, const void* w_gate, const void* w_up, con
                               int64_t y_row_stride_elems, void* workspace,
                               int64_t workspace_bytes, unsigned flags, void* stream);
 
+/* The same MoE layer for callers that cannot allocate device memory when they
+ * call in: a plain C host handed device pointers with no allocator of its own,
+ * a serving loop that must not hit cudaMalloc mid-step (it may synchronize the
+ * device), or code whose device memory belongs to a caching allocator or a
+ * pre-planned arena.  No counterpart in the reference (it has no MoE and its
+ * shims allocate nothing device-side).
+ * Scratch is a static 8 MiB array inside the library, reserved on every GPU
+ * that loads the library until the process exits; this call allocates
+ * nothing.  Dims whose spiral_moe_workspace_bytes exceeds 8 MiB are rejected
+ * with SPIRAL_ERR_CAPACITY (config-4 dims, 128 experts x hidden 2048 x inter
+ * 768 at top-8, fit up to 107 tokens).  The first call on a device looks up
+ * the array's device address; make that first call before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race on
+ * it, so order them (one stream, or events).  Arguments as spiral_moe_ffn
+ * without the workspace. */
+SPIRAL_API int spiral_moe_ffn_noalloc(int fmt, const void* w_gate, const void* w_up,
+                                      const void* w_down, int64_t n_experts_local,
+                                      int64_t expert_first, int64_t hidden, int64_t inter,
+                                      const void* x, int64_t x_row_stride_elems, int64_t tokens,
+                                      const int32_t* expert_ids, const float* expert_weights,
+                                      int64_t topk, void* y, int y_dtype,
+                                      int64_t y_row_stride_elems, unsigned flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

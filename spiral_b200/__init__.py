@@ -47,6 +47,8 @@ _SIGNATURES = {
     "spiral_moe_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64], _i64),
     "spiral_moe_ffn": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i32,
                         _i64, _vp, _i64, _u32, _vp], _i32),
+    "spiral_moe_ffn_noalloc": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp,
+                                _i32, _i64, _u32, _vp], _i32),
 }
 
 _lib = None

@@ -342,6 +342,27 @@ int spiral_moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w_
   return SPIRAL_OK;
 }
 
+int spiral_moe_ffn_noalloc(int fmt, const void* w_gate, const void* w_up, const void* w_down, int64_t n_experts_local,
+                           int64_t expert_first, int64_t hidden, int64_t inter, const void* x,
+                           int64_t x_row_stride_elems, int64_t tokens, const int32_t* expert_ids,
+                           const float* expert_weights, int64_t topk, void* y, int y_dtype,
+                           int64_t y_row_stride_elems, unsigned flags, void* stream) {
+  g_last_error[0] = 0;
+  const int64_t need = spiral_moe_workspace_bytes(n_experts_local, hidden, inter, tokens, topk);
+  const int64_t cap = static_cast<int64_t>(moe_noalloc_scratch_bytes());
+  if (need > cap)
+    return fail(SPIRAL_ERR_CAPACITY,
+                "these dims need %lld bytes of scratch; the allocation-free entry point has %lld (use "
+                "spiral_moe_ffn with a workspace)",
+                (long long)need, (long long)cap);
+  void* scratch = nullptr;
+  const cudaError_t e = moe_noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "static scratch address");
+  return spiral_moe_ffn(fmt, w_gate, w_up, w_down, n_experts_local, expert_first, hidden, inter, x,
+                        x_row_stride_elems, tokens, expert_ids, expert_weights, topk, y, y_dtype, y_row_stride_elems,
+                        scratch, cap, flags, stream);
+}
+
 int spiral_device_status(void* stream, uint32_t* code) {
   g_last_error[0] = 0;
   if (code == nullptr) return fail(SPIRAL_ERR_NULL_POINTER, "null code");

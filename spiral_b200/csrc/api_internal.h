@@ -53,6 +53,11 @@ cudaError_t moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w
                     bool accumulate, bool ftz, int64_t T, int64_t topk, int64_t H, int64_t I, int64_t e0,
                     int64_t E_local, void* ws, cudaStream_t stream);
 
+// Allocation-free MoE: capacity and device address (current device) of the
+// library's static scratch array.
+size_t moe_noalloc_scratch_bytes();
+cudaError_t moe_noalloc_scratch(void** ptr);
+
 // Device properties cached per device.
 int device_sm_count();
 size_t device_max_smem_optin();

@@ -32,6 +32,7 @@
 // Scratch (counts, pair lists, problem table, h, per-pair outputs) lives in a
 // caller-provided workspace (spiral_moe_workspace_bytes).
 #include <atomic>
+#include <mutex>
 
 #include "api_internal.h"
 #include "gemv_decode.cuh"
@@ -525,6 +526,49 @@ cudaError_t moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w
     case kQ6_K: return moe_run<kQ6_K>(a, stream);
   }
   return cudaErrorInvalidValue;
+}
+
+// ------------------------------------------------ allocation-free variant ----
+//
+// spiral_moe_ffn_noalloc serves callers that cannot allocate device memory
+// at the point where they call in: a host without a device allocator of its
+// own (a plain C program handed device pointers), a serving loop that must
+// not hit cudaMalloc mid-step (it may synchronize the device), or code whose
+// device memory is owned by a caching allocator or a pre-planned arena that
+// a stray allocation would disturb.  Its scratch is this file-scope array,
+// reserved on every GPU that loads the library until the process exits.
+// Every call shares it and it keeps the last call's contents: the MoE layer
+// reads only scratch bytes it wrote earlier in the same call, so nothing has
+// to start at zero; calls that overlap on the GPU (different streams, or
+// host threads without ordering between them) race on it.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per GPU
+static __device__ __align__(256) uint8_t g_moe_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+}  // namespace
+
+size_t moe_noalloc_scratch_bytes() { return kNoAllocScratchBytes; }
+
+// Device address of the array on the current device.  The first call on a
+// device looks it up (cudaGetSymbolAddress, with that device current); in
+// host code the array's name is only a stand-in for the symbol, never a
+// device address.
+cudaError_t moe_noalloc_scratch(void** ptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_moe_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_addr[dev] = p;
+  }
+  *ptr = g_noalloc_addr[dev];
+  return cudaSuccess;
 }
 
 }  // namespace spiral
