@@ -54,16 +54,24 @@ __global__ void __launch_bounds__(kDequantWarps * 32)
   if (g0 >= total_groups) return;
   uint8_t* buf = sbuf[warp];
 
+  // One 32-bit division per unit (the host guarantees total_groups < 2^32);
+  // the unit's later groups step along the row and wrap to the next rows.
   int64_t src_off[U::kGroups], dst_off[U::kGroups];
   bool valid[U::kGroups];
+  {
+    const uint32_t gpr = static_cast<uint32_t>(groups_per_row);
+    uint32_t row = static_cast<uint32_t>(g0) / gpr;
+    uint32_t gi = static_cast<uint32_t>(g0) - row * gpr;
 #pragma unroll
-  for (int g = 0; g < U::kGroups; ++g) {
-    const int64_t gg = g0 + g;
-    valid[g] = gg < total_groups;
-    const int64_t row = valid[g] ? gg / groups_per_row : 0;
-    const int64_t gi = valid[g] ? gg - row * groups_per_row : 0;
-    src_off[g] = row * src_stride + gi * U::kGroupBytes;
-    dst_off[g] = row * dst_stride + gi * U::kGroupK;
+    for (int g = 0; g < U::kGroups; ++g) {
+      valid[g] = g0 + g < total_groups;
+      src_off[g] = static_cast<int64_t>(row) * src_stride + static_cast<int64_t>(gi) * U::kGroupBytes;
+      dst_off[g] = static_cast<int64_t>(row) * dst_stride + static_cast<int64_t>(gi) * U::kGroupK;
+      if (++gi == gpr) {
+        gi = 0;
+        ++row;
+      }
+    }
   }
 
   constexpr int kPieces = U::kGroupBytes / 16;
@@ -220,11 +228,16 @@ bool dequant_fast_ok(int fmt, const void* src, int64_t src_stride, const void* d
          (src_stride % 16 == 0) && ((dst_stride * 2) % 16 == 0) && (K % gk == 0);
 }
 
+static bool dequant_fast_fits(int fmt, int64_t K, int64_t N) {
+  const int64_t gk = fmt == kQ6_K ? 2048 : 256;
+  return (K / gk) * N < (int64_t(1) << 32) - 8;  // 32-bit group indices
+}
+
 cudaError_t dequant_rows(int fmt, const void* src, int64_t src_stride, void* dst, int64_t dst_stride, int64_t K,
                          int64_t N, bool ftz, cudaStream_t stream) {
   const auto* s = static_cast<const uint8_t*>(src);
   auto* d = static_cast<uint16_t*>(dst);
-  const bool fast = dequant_fast_ok(fmt, src, src_stride, dst, dst_stride, K);
+  const bool fast = dequant_fast_ok(fmt, src, src_stride, dst, dst_stride, K) && dequant_fast_fits(fmt, K, N);
 #define SPIRAL_DQ(F)                                                                   \
   return ftz ? launch_rows<F, true>(s, src_stride, d, dst_stride, K, N, fast, stream) \
              : launch_rows<F, false>(s, src_stride, d, dst_stride, K, N, fast, stream)
