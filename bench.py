@@ -280,7 +280,7 @@ def run_spiral(args):
 
     fid = F.BY_NAME[args.fmt]
     K, N = K_DIM, N_DIM
-    from spiral_b200.dist import gather_rows, row_range
+    from spiral_b200.dist import PeerOutputs, gather_rows, row_range
 
     n0, n1 = row_range(N, world, rank)
     Nr = n1 - n0
@@ -295,18 +295,29 @@ def run_spiral(args):
     xs = {B: torch.from_numpy(F.gen_activations(B, K, seed=100 + B).view(np.int16)).to(dev).view(torch.bfloat16)
           for B in BATCHES}
     ys = {B: torch.empty((B, Nr), dtype=torch.bfloat16, device=dev) for B in BATCHES}
-    yfull = {}
+    # N > 1: the GEMV stores its shard straight into every rank's full output
+    # (peer memory over NVLink) and signals; one output per batch size, so
+    # consecutive calls never share a buffer
+    po = PeerOutputs({B: (B, N) for B in BATCHES}, dev) if world > 1 else None
+
+    def mul_mat_full(w, xb, B):
+        if world > 1:
+            sp.mul_mat_allgather(fid, w, xb, Nr, K, po.y_peers[B], N, n0, po.signals, rank, world)
+            return po.y[B]
+        sp.mul_mat(fid, w, xb, Nr, K, ys[B], y_dtype=sp.BF16, static_weights=True)
+        return ys[B]
 
     # every MUL_MAT of the sweep reads a different weight copy, so no launch
     # finds its weights in L2 (the last use of a copy is `copies` launches ago)
-    def sweep(i, x=None, y=None):
+    def sweep(i):
+        for j, B in enumerate(BATCHES):
+            mul_mat_full(weights[(i * len(BATCHES) + j) % copies], xs[B], B)
+
+    def sweep_nccl(i):  # the same step with a separate NCCL all-gather (comparison only)
         for j, B in enumerate(BATCHES):
             w = weights[(i * len(BATCHES) + j) % copies]
-            xb = xs[B] if x is None else x[B]
-            yb = ys[B] if y is None else y[B]
-            sp.mul_mat(fid, w, xb, Nr, K, yb, y_dtype=sp.BF16, static_weights=True)
-            if world > 1:
-                yfull[B] = gather_rows(yb, N)
+            sp.mul_mat(fid, w, xs[B], Nr, K, ys[B], y_dtype=sp.BF16, static_weights=True)
+            gather_rows(ys[B], N)
 
     stream = torch.cuda.Stream(device=dev)
     # warm-up (also configures kernel attributes and the per-stream GEMV
@@ -315,6 +326,8 @@ def run_spiral(args):
         sweep(i)
     with torch.cuda.stream(stream):
         sweep(0)
+        if world > 1:
+            sweep_nccl(0)
     torch.cuda.synchronize()
     graph_steps = copies if copies <= 64 else 64
 
@@ -398,17 +411,20 @@ def run_spiral(args):
         for j, B in enumerate(BATCHES):
             w = weights[(i * len(BATCHES) + j) % copies]
             xd[B].view(torch.int16).copy_(hx[B], non_blocking=True)
-            sp.mul_mat(fid, w, xd[B], Nr, K, ys[B], y_dtype=sp.BF16, static_weights=True)
-            if world > 1:
-                hy[B].view(B, N).copy_(gather_rows(ys[B], N).view(torch.int16), non_blocking=True)
-            else:
-                hy[B].copy_(ys[B].view(torch.int16), non_blocking=True)
+            hy[B].copy_(mul_mat_full(w, xd[B], B).view(torch.int16), non_blocking=True)
 
     e2e_steps = max(graph_steps, args.steps // 4)
     ms_e2e = timed(e2e_steps, 3, sweep_e2e, {})
     e2e_value = wbytes_step / (ms_e2e / e2e_steps * 1e-3) / 1e9
     h2d = sum(B * K * 2 for B in BATCHES)
     d2h = sum(B * N * 2 for B in BATCHES)
+
+    nccl = None
+    if world > 1:
+        msn = timed(e2e_steps, 3, sweep_nccl, {})
+        nccl = {"value": wbytes_step / (msn / e2e_steps * 1e-3) / 1e9, "unit": "GB/s",
+                "ms_per_step": msn / e2e_steps,
+                "note": "same step with spiral_mul_mat + torch.distributed all_gather_into_tensor (NCCL)"}
 
     extras = {}
     if world == 1 and not args.no_extras:
@@ -442,22 +458,26 @@ def run_spiral(args):
                        "weight_copies": copies,
                        "l2": f"inputs larger than L2: {copies} rotating weight copies "
                              f"({copies * shard_bytes / 2**20:.0f} MiB per rank > 126 MB L2)",
-                       "parallelism": "single GPU" if world == 1 else f"row-shard x{world} + NCCL all-gather",
+                       "parallelism": "single GPU" if world == 1 else
+                       f"row-shard x{world}, all-gather fused into the GEMV (NVLink peer stores + signal)",
                        "graphs": f"CUDA graphs of {graph_steps} steps"},
             "roofline": roofline,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "note": "public C-ABI, pinned host x in / y out every step, weights resident"},
-            "gpu_launches": args.steps * len(BATCHES),
+            "gpu_launches": args.steps * len(BATCHES) * (1 if world == 1 else 2),
             "clocks": clk.summary(),
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
         if extras:
             line["extras"] = extras
+        if nccl is not None:
+            line["nccl_allgather_baseline"] = nccl
         print(json.dumps(line), flush=True)
 
     del main_cache
     if world > 1:
+        del po
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -193,6 +193,33 @@ SPIRAL_API int spiral_mul_mat(int fmt, const void* w, int64_t w_row_stride_bytes
                    int y_dtype, int64_t y_row_stride_elems, int64_t M,
                    int64_t N, int64_t K, unsigned flags, void* stream);
 
+/* Row-sharded MUL_MAT with the output all-gather fused into the kernel, for
+ * one process per GPU (BASELINE config 2 at 2..8 GPUs; the reference has no
+ * multi-device path — its multi-tile pattern splits weights by output column
+ * and broadcasts the input, src/quants/tests/poc/calc.py:1-11, 154-215).
+ * This rank computes y[m][n_offset + n] = sum_k bf16(Wshard[n][k]) x[m][k],
+ * n < N_shard, m < M <= 8, and stores every bf16 output straight into the
+ * full output of every rank (y_peers[r] + m * y_row_stride_elems +
+ * n_offset + n, peer memory over NVLink); its last CTA then adds 1 to
+ * signal_peers[r][rank] on every rank r and waits (bounded) for, and
+ * consumes, one arrival from every rank, so the kernel completes only with
+ * the whole gathered output in this rank's memory and work queued after it
+ * on the stream sees all of it.
+ * y_peers, signal_peers: DEVICE arrays of `world` device pointers (e.g. from
+ * a symmetric-memory rendezvous); every y_peers[r] 16-byte aligned,
+ * y_row_stride_elems and n_offset multiples of 8; each rank's signal block
+ * holds world + 1 uint32, zero before the first call.  Every rank must make
+ * the same calls in the same order.  A call can store into a peer's buffer
+ * once that peer has finished the GEMV of its previous call, so two output
+ * buffers used alternately are safe when every consumer of an output is
+ * queued on the stream before the next call. */
+SPIRAL_API int spiral_mul_mat_allgather(int fmt, const void* w_shard, int64_t w_row_stride_bytes,
+                                        const void* x, int64_t x_row_stride_elems,
+                                        void* const* y_peers, int64_t y_row_stride_elems,
+                                        int64_t n_offset, int64_t M, int64_t N_shard, int64_t K,
+                                        uint32_t* const* signal_peers, int rank, int world,
+                                        unsigned flags, void* stream);
+
 /* Fused unpack + mmul in the reference's tiled I/O orders:
  *   inputs  bf16 [weights_rows/8][inputs_vecs][8]
  *   outputs f32  [weights_cols/8][inputs_vecs][8], ACCUMULATED (+=); the

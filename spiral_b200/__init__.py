@@ -44,6 +44,8 @@ _SIGNATURES = {
     "spiral_quants_unpack_all": ([_i32, _vp, _vp, _i64, _i64, _u32, _vp], _i32),
     "spiral_mul_mat": ([_i32, _vp, _i64, _vp, _i64, _vp, _i32, _i64, _i64, _i64, _i64, _u32, _vp], _i32),
     "spiral_quants_unpack_mmul_all": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _u32, _vp], _i32),
+    "spiral_mul_mat_allgather": ([_i32, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i32, _i32,
+                                  _u32, _vp], _i32),
     "spiral_moe_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64], _i64),
     "spiral_moe_ffn": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i32,
                         _i64, _vp, _i64, _u32, _vp], _i32),
@@ -198,6 +200,20 @@ def unpack_mmul_all(fmt, packed, inputs_tiled, outputs, weights_rows: int, weigh
                                                weights_rows, weights_cols, inputs_vecs,
                                                FLAG_FTZ_SCALES if ftz else 0, _stream(stream)))
     return outputs
+
+
+def mul_mat_allgather(fmt, w_shard, x, N_shard: int, K: int, y_peers_dev, y_row_stride: int, n_offset: int,
+                      signal_peers_dev, rank: int, world: int, *, w_row_stride: int | None = None,
+                      ftz: bool = False, static_weights: bool = True, stream=None):
+    """Row-sharded MUL_MAT whose bf16 outputs land in every rank's full
+    output (peer stores) before the call's in-stream wait returns; see
+    spiral_b200.dist.PeerOutputs for the buffers."""
+    f = fmt_id(fmt)
+    M = int(x.shape[0])
+    flags = (FLAG_FTZ_SCALES if ftz else 0) | (FLAG_STATIC_WEIGHTS if static_weights else 0)
+    _check(lib().spiral_mul_mat_allgather(f, _ptr(w_shard), w_row_stride or row_bytes(f, K), _ptr(x),
+                                          int(x.stride(0)), _ptr(y_peers_dev), y_row_stride, n_offset, M, N_shard, K,
+                                          _ptr(signal_peers_dev), rank, world, flags, _stream(stream)))
 
 
 # ---------------------------------------------------------------- MoE FFN

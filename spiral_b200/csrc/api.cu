@@ -294,6 +294,49 @@ int spiral_quants_unpack_mmul_all(int fmt, const void* packed, const void* input
   return run_mat(a, static_cast<cudaStream_t>(stream));
 }
 
+int spiral_mul_mat_allgather(int fmt, const void* w_shard, int64_t w_row_stride_bytes, const void* x,
+                             int64_t x_row_stride_elems, void* const* y_peers, int64_t y_row_stride_elems,
+                             int64_t n_offset, int64_t M, int64_t N_shard, int64_t K, uint32_t* const* signal_peers,
+                             int rank, int world, unsigned flags, void* stream) {
+  g_last_error[0] = 0;
+  if (int st = check_shape(fmt, K, N_shard)) return st;
+  if (M <= 0 || M > 8) return fail(SPIRAL_ERR_INVALID_SHAPE, "M=%lld: the gathered GEMV takes 1..8 vectors", (long long)M);
+  if (world < 1 || world > 64 || rank < 0 || rank >= world)
+    return fail(SPIRAL_ERR_INVALID_ARGUMENT, "rank %d / world %d", rank, world);
+  if (!w_shard || !x || !y_peers || !signal_peers) return fail(SPIRAL_ERR_NULL_POINTER, "null operand");
+  if (n_offset < 0 || y_row_stride_elems < n_offset + N_shard)
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "shard columns [%lld, %lld) outside the output row of %lld",
+                (long long)n_offset, (long long)(n_offset + N_shard), (long long)y_row_stride_elems);
+  if (w_row_stride_bytes < row_bytes(fmt, K) || x_row_stride_elems < K)
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "w/x row strides smaller than a row");
+  if ((reinterpret_cast<uintptr_t>(w_shard) & 15u) || (w_row_stride_bytes & 15) || (reinterpret_cast<uintptr_t>(x) & 1u))
+    return fail(SPIRAL_ERR_ALIGNMENT, "weights need 16-byte aligned rows");
+  if ((y_row_stride_elems & 7) || (n_offset & 7))
+    return fail(SPIRAL_ERR_ALIGNMENT, "output row stride and shard offset must be multiples of 8 elements");
+  MatArgs a{};
+  a.fmt = fmt;
+  a.w = static_cast<const uint8_t*>(w_shard);
+  a.w_stride = w_row_stride_bytes;
+  a.x = static_cast<const uint16_t*>(x);
+  a.x_s8 = 8;
+  a.x_sm = x_row_stride_elems;
+  a.y = nullptr;
+  a.y_s8 = 8;
+  a.y_sm = y_row_stride_elems;
+  a.y_bf16 = true;
+  a.ftz = (flags & SPIRAL_FLAG_FTZ_SCALES) != 0;
+  a.static_weights = (flags & SPIRAL_FLAG_STATIC_WEIGHTS) != 0;
+  a.M = M;
+  a.N = N_shard;
+  a.K = K;
+  PeerOut po{y_peers, signal_peers, n_offset, rank, world};
+  const cudaError_t e = gemv_allgather(a, po, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorNotSupported)
+    return fail(SPIRAL_ERR_UNSUPPORTED, "shape not served by the pipelined GEMV (K=%lld)", (long long)K);
+  if (e != cudaSuccess) return cuda_fail(e, "gathered gemv launch");
+  return SPIRAL_OK;
+}
+
 int64_t spiral_moe_workspace_bytes(int64_t n_experts_local, int64_t hidden, int64_t inter, int64_t tokens,
                                    int64_t topk) {
   if (n_experts_local <= 0 || hidden <= 0 || inter <= 0 || tokens <= 0 || topk <= 0) return 0;

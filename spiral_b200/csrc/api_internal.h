@@ -41,6 +41,18 @@ struct MatArgs {
 bool gemv_fast_ok(const MatArgs& a);
 cudaError_t gemv(const MatArgs& a, cudaStream_t stream);
 
+// Row-sharded GEMV whose epilogue stores into every rank's full output
+// (peer memory over NVLink) and signals; then an in-stream bounded wait for
+// every rank's shard.  y_peers / sig_peers are device arrays of `world`
+// pointers; each rank's signal words hold world + 1 uint32, zero at start.
+struct PeerOut {
+  void* const* y_peers;
+  uint32_t* const* sig_peers;
+  int64_t n_offset;
+  int rank, world;
+};
+cudaError_t gemv_allgather(const MatArgs& a, const PeerOut& po, cudaStream_t stream);
+
 // gemm.cu — tcgen05 dequant-GEMM for larger M.
 bool gemm_supported(const MatArgs& a);
 cudaError_t gemm(const MatArgs& a, cudaStream_t stream);

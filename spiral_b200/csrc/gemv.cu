@@ -72,6 +72,14 @@ struct GemvParams {
   int x_pitch;    // bytes per activation vector in the permuted copy
   int y_bf16, accumulate, ftz;
   int static_weights;  // weights may be read before the preceding grid ends
+  // Peer output (world > 0): every output goes to column n_offset + n of
+  // each rank's full output (y_peers[r], bf16, row stride y_sm); the last CTA
+  // then raises this rank's counter on every rank (sig_peers[r][rank]) and
+  // consumes one arrival of every rank from its own counters.
+  void* const* y_peers;
+  uint32_t* const* sig_peers;
+  int64_t n_offset;
+  int rank, world;
 };
 
 // ------------------------------------------------- activation staging ----
@@ -261,7 +269,28 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
       const int row = (l >> 2) + 8 * (j >> 1);
       const int m = 2 * (l & 3) + (j & 1);
       const int64_t n = tile * kTileRows + row;
-      if (m < p.M && n < p.N) {
+      if (p.world > 0) {
+        // Peer output: the tile's bf16 outputs are gathered in shared memory
+        // (the reduction slots, free once every sum is read) as [m][16 rows],
+        // then leave in 16-byte pieces, one per (rank, m, half-tile).
+        uint16_t* tile_out = reinterpret_cast<uint16_t*>(gred);
+        named_bar_sync(kGroupsPerCta + 2 + grp, 128);
+        tile_out[m * kTileRows + row] = static_cast<uint16_t>(pack_bf16x2(sum, 0.f) & 0xFFFFu);
+        named_bar_sync(kGroupsPerCta + 2 + grp, 128);
+        const int items = p.M * 2 * p.world;
+        for (int it = t; it < items; it += 128) {
+          const int half = it & 1, mm = (it >> 1) % p.M, rr = (it >> 1) / p.M;
+          const int64_t n0 = tile * kTileRows + half * 8;
+          if (n0 >= p.N) continue;
+          uint16_t* dst = static_cast<uint16_t*>(p.y_peers[rr]) + static_cast<int64_t>(mm) * p.y_sm + p.n_offset + n0;
+          const uint16_t* src = tile_out + mm * kTileRows + half * 8;
+          if (n0 + 8 <= p.N) {
+            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+          } else {
+            for (int e = 0; e < p.N - n0; ++e) dst[e] = src[e];
+          }
+        }
+      } else if (m < p.M && n < p.N) {
         const int64_t off = (n >> 3) * p.y_s8 + static_cast<int64_t>(m) * p.y_sm + (n & 7);
         if (p.y_bf16) {
           static_cast<uint16_t*>(p.y)[off] = static_cast<uint16_t>(pack_bf16x2(sum, 0.f) & 0xFFFFu);
@@ -273,6 +302,50 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
       }
     }
     named_bar_sync(1 + grp, kWarpsPerGroup * 32);
+  }
+  if (p.world > 0) {
+    // Every output of this CTA is stored (to all ranks) before it counts
+    // itself done.  The CTA that completes the count tells every rank, after
+    // a system-scope fence, that this rank's shard has landed, then waits
+    // (bounded) for one arrival from every rank and consumes it: the grid
+    // completes only once the whole output is in this rank's memory, so
+    // stream order alone covers every later reader.  Each rank signals
+    // before it waits, so the waits cannot cycle.  A CTA whose pipeline gave
+    // up marks the count (bit 31) and no rank is signalled: their bounded
+    // waits then report the failure instead of passing on a partial shard.
+    // The next call's CTAs add to the count only after this grid completed
+    // (their consumers wait for it), so the reset below is never raced.
+    named_bar_sync(kGroupsPerCta + 1, kConsumerWarps * 32);
+    if (threadIdx.x == 0) {
+      __threadfence_system();  // cumulative: covers the CTA's stores ordered before the barrier
+      uint32_t* mine = p.sig_peers[p.rank];
+      uint32_t* done = mine + p.world;
+      if (*(volatile int*)&abort_flag) atomicOr(done, 0x80000000u);
+      const uint32_t before = atomicAdd(done, 1u);
+      if ((before & 0x7FFFFFFFu) == gridDim.x - 1) {
+        *done = 0u;
+        __threadfence_system();
+        if (!(before & 0x80000000u)) {
+          for (int rr = 0; rr < p.world; ++rr) atomicAdd_system(p.sig_peers[rr] + p.rank, 1u);
+        }
+        for (int rr = 0; rr < p.world; ++rr) {
+          const uint64_t t0 = globaltimer_ns();
+          bool arrived = true;
+          for (;;) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + rr) : "memory");
+            if (v >= 1u) break;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              raise_device_error(kDevErrMbarTimeout);
+              arrived = false;
+              break;
+            }
+          }
+          if (!arrived) break;
+          atomicSub(mine + rr, 1u);
+        }
+      }
+    }
   }
 }
 
@@ -382,10 +455,11 @@ bool gemv_fast_ok(const MatArgs& a) {
 }
 
 template <int FMT>
-static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream) {
+static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream, const PeerOut* po = nullptr) {
   using F = GemvFmt<FMT>;
   GemvPlan plan;
   if (reinterpret_cast<uintptr_t>(a.w) % 16 != 0 || a.w_stride % 16 != 0 || !gemv_plan<FMT>(a, &plan)) {
+    if (po != nullptr) return cudaErrorNotSupported;
     const int64_t blocks = std::min<int64_t>((a.N + 7) / 8, int64_t(device_sm_count()) * 16);
     gemv_generic<FMT><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
     return cudaGetLastError();
@@ -412,6 +486,13 @@ static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream) {
   p.accumulate = a.accumulate;
   p.ftz = a.ftz;
   p.static_weights = a.static_weights;
+  if (po != nullptr) {
+    p.y_peers = po->y_peers;
+    p.sig_peers = po->sig_peers;
+    p.n_offset = po->n_offset;
+    p.rank = po->rank;
+    p.world = po->world;
+  }
 
   int dev = 0;
   cudaGetDevice(&dev);
@@ -444,6 +525,15 @@ cudaError_t gemv(const MatArgs& a, cudaStream_t stream) {
     case kQ4_0: return gemv_t<kQ4_0>(a, stream);
     case kQ8_0: return gemv_t<kQ8_0>(a, stream);
     case kQ6_K: return gemv_t<kQ6_K>(a, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t gemv_allgather(const MatArgs& a, const PeerOut& po, cudaStream_t stream) {
+  switch (a.fmt) {
+    case kQ4_0: return gemv_t<kQ4_0>(a, stream, &po);
+    case kQ8_0: return gemv_t<kQ8_0>(a, stream, &po);
+    case kQ6_K: return gemv_t<kQ6_K>(a, stream, &po);
   }
   return cudaErrorInvalidValue;
 }

@@ -102,3 +102,34 @@ def moe_dispatch_combine(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tens
             y.index_add_(0, send_tok[d], part_back[off:off + n])
         off += n
     return y
+
+
+class PeerOutputs:
+    """Full-size bf16 output buffers that every rank can store into, for
+    spiral_b200.mul_mat_allgather: one symmetric-memory allocation per rank
+    (torch.distributed._symmetric_memory, peer-mapped over NVLink) holding an
+    [M][N] bf16 output per key plus the signal words, and device arrays of the
+    peers' pointers.  Collective: every rank constructs it with the same
+    shapes."""
+
+    def __init__(self, shapes: dict, device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        offs, off = {}, 0
+        for key, (m, n) in shapes.items():
+            offs[key] = off
+            off += ((m * n * 2 + 255) // 256) * 256
+        sig_off = off
+        total = sig_off + 256 * ((4 * (self.world + 1) + 255) // 256)
+        self._buf = symm_mem.empty(total, dtype=torch.uint8, device=device)
+        self._buf.zero_()
+        self._hdl = symm_mem.rendezvous(self._buf, group=group if group is not None else dist.group.WORLD)
+        ptrs = list(self._hdl.buffer_ptrs)
+        self.signals = torch.tensor([p + sig_off for p in ptrs], dtype=torch.int64, device=device)
+        self.y_peers, self.y = {}, {}
+        for key, (m, n) in shapes.items():
+            self.y_peers[key] = torch.tensor([p + offs[key] for p in ptrs], dtype=torch.int64, device=device)
+            self.y[key] = self._buf[offs[key]:offs[key] + m * n * 2].view(torch.bfloat16).view(m, n)
+        dist.barrier(group=group)

@@ -163,3 +163,29 @@ def test_moe_validation_codes():
     assert call(ws=260) == -4
     assert call(wsb=1024) == -5  # workspace too small
     assert call(yd=7) == -10
+
+
+def test_mul_mat_allgather_validation_codes():
+    L = sp.lib()
+
+    def call(**kw):
+        a = dict(fmt=sp.Q4_0, w=256, ws=2304, x=256, xs=4096, yp=256, ys=14336, off=7168, M=8, N=7168, K=4096,
+                 sig=256, rank=1, world=2, flags=0)
+        a.update(kw)
+        return L.spiral_mul_mat_allgather(a["fmt"], a["w"], a["ws"], a["x"], a["xs"], a["yp"], a["ys"], a["off"],
+                                          a["M"], a["N"], a["K"], a["sig"], a["rank"], a["world"], a["flags"], 0)
+
+    assert call(fmt=3) == -1
+    assert call(K=4001) == -2
+    assert call(M=9) == -2 and b"1..8" in L.spiral_last_error()
+    assert call(M=0) == -2
+    assert call(rank=2) == -10
+    assert call(world=0) == -10
+    assert call(yp=0) == -3
+    assert call(sig=0) == -3
+    assert call(off=7169) == -2  # shard runs past the output row
+    assert call(off=-1) == -2
+    assert call(ws=2000) == -2
+    assert call(w=264) == -4
+    assert call(off=4) == -4  # 16-byte output pieces
+    assert call(ys=14340) == -4

@@ -1,5 +1,6 @@
 """Multi-GPU paths on 2 B200s (skipped with fewer GPUs): the row-sharded
-dequant-GEMV with an NCCL all-gather, and the expert-parallel MoE layer with
+dequant-GEMV with an NCCL all-gather and with the all-gather fused into the
+kernel (NVLink peer stores), and the expert-parallel MoE layer with
 NCCL all-to-all dispatch and combine, each rank running libspiral_b200 on its
 own GPU.  Checked against the float64 oracle of the whole operation."""
 
@@ -56,6 +57,30 @@ def _worker(rank, world, port, q):
         y = gather_rows(y_local, N).cpu().numpy()
         ok_dense, rel_dense = tolerance_ok(y, oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=False)
 
+        # the same GEMV with the all-gather fused in (peer stores + signals),
+        # uneven shards (113 tiles of 16 rows over 2 ranks), every batch size,
+        # two buffers used alternately, several calls in a row
+        from spiral_b200.dist import PeerOutputs
+
+        Ng = 1808
+        rawg = F.generate(fid, K, Ng, seed=7)
+        g0, g1 = row_range(Ng, world, rank)
+        wg_shard = torch.from_numpy(rawg[g0 * rb:g1 * rb]).to(dev)
+        po = PeerOutputs({(B, s): (B, Ng) for B in (1, 2, 5, 8) for s in (0, 1)}, dev)
+        ok_fused, rel_fused = True, 0.0
+        for it in range(6):
+            B = (1, 2, 5, 8)[it % 4]
+            xb = F.gen_activations(B, K, seed=20 + it)
+            xdb = torch.from_numpy(xb.view(np.int16)).to(dev).view(torch.bfloat16)
+            sp.mul_mat_allgather(fid, wg_shard, xdb, g1 - g0, K, po.y_peers[(B, it % 2)], Ng, g0, po.signals, rank,
+                                 world)
+            yg = po.y[(B, it % 2)].float().cpu().numpy()
+            ok, rel = tolerance_ok(yg, oracle.mul_mat_f64(fid, rawg, xb, K, Ng), bf16_out=True)
+            ok_fused, rel_fused = ok_fused and ok, max(rel_fused, rel)
+        torch.cuda.synchronize()
+        dist.barrier()
+        del po
+
         # MoE: 16 Q4_0 experts, hidden 512, inter 256, top-4, tokens sharded
         E, H, I, T, topk = 16, 512, 256, 9, 4
         wg = F.gen_experts(fid, E, I, H, seed=1)
@@ -79,7 +104,7 @@ def _worker(rank, world, port, q):
                                   compute)
         ref = oracle.moe_ffn_f64(fid, wg, wu, wdn, xm, ids, wts, H, I, E)[t0:t1]
         ok_moe, rel_moe = tolerance_ok(ym.cpu().numpy(), ref, bf16_out=False, rel_tol=2e-3)
-        q.put((rank, ok_dense, rel_dense, ok_moe, rel_moe, sp.device_status()))
+        q.put((rank, ok_dense, rel_dense, ok_moe, rel_moe, ok_fused, rel_fused, sp.device_status()))
     finally:
         dist.destroy_process_group()
 
@@ -97,7 +122,8 @@ def test_two_gpu_row_shard_and_expert_parallel_moe():
     for p in procs:
         p.join(timeout=300)
     assert [p.exitcode for p in procs] == [0, 0]
-    for rank, ok_d, rel_d, ok_m, rel_m, status in (q.get() for _ in range(2)):
+    for rank, ok_d, rel_d, ok_m, rel_m, ok_f, rel_f, status in (q.get() for _ in range(2)):
         assert ok_d, (rank, rel_d)
+        assert ok_f, (rank, rel_f)
         assert ok_m, (rank, rel_m)
         assert status == 0
