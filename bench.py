@@ -280,7 +280,7 @@ def run_spiral(args):
 
     fid = F.BY_NAME[args.fmt]
     K, N = K_DIM, N_DIM
-    from spiral_b200.dist import PeerOutputs, gather_rows, row_range
+    from spiral_b200.dist import AllGatherExchange, gather_rows, row_range
 
     n0, n1 = row_range(N, world, rank)
     Nr = n1 - n0
@@ -295,15 +295,15 @@ def run_spiral(args):
     xs = {B: torch.from_numpy(F.gen_activations(B, K, seed=100 + B).view(np.int16)).to(dev).view(torch.bfloat16)
           for B in BATCHES}
     ys = {B: torch.empty((B, Nr), dtype=torch.bfloat16, device=dev) for B in BATCHES}
-    # N > 1: the GEMV stores its shard straight into every rank's full output
-    # (peer memory over NVLink) and signals; one output per batch size, so
-    # consecutive calls never share a buffer
-    po = PeerOutputs({B: (B, N) for B in BATCHES}, dev) if world > 1 else None
+    # N > 1: the GEMV sends its shard to every other rank over NVLink and
+    # gathers theirs into its own full output (spiral_mul_mat_allgather)
+    xc = AllGatherExchange(N, dev) if world > 1 else None
+    yfull = {B: torch.empty((B, N), dtype=torch.bfloat16, device=dev) for B in BATCHES}
 
     def mul_mat_full(w, xb, B):
         if world > 1:
-            sp.mul_mat_allgather(fid, w, xb, Nr, K, po.y_peers[B], N, n0, po.signals, rank, world)
-            return po.y[B]
+            sp.mul_mat_allgather(fid, w, xb, Nr, K, yfull[B], n0, xc.peers, rank, world)
+            return yfull[B]
         sp.mul_mat(fid, w, xb, Nr, K, ys[B], y_dtype=sp.BF16, static_weights=True)
         return ys[B]
 
@@ -324,11 +324,16 @@ def run_spiral(args):
     # scratch before any capture; graphs are captured on `stream`)
     for i in range(3):
         sweep(i)
+    # the side stream must not overlap the default stream's calls (gathered
+    # calls on one exchange are strictly ordered)
+    torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         sweep(0)
         if world > 1:
             sweep_nccl(0)
     torch.cuda.synchronize()
+    if sp.device_status() != 0:
+        raise SystemExit(f"rank {rank}: a device-side wait gave up during warm-up")
     graph_steps = copies if copies <= 64 else 64
 
     def capture(nsteps, start, body):
@@ -440,6 +445,10 @@ def run_spiral(args):
                "sample": f"{reps} full sweeps (B=1,2,4,8) over {rows}x{K} {args.fmt} in "
                          f"~{args.cpu_seconds:.0f} s, oracle/oracle.c OpenMP"}
 
+    status = sp.device_status()
+    if status != 0:
+        raise SystemExit(f"rank {rank}: device status {status} after the timed runs")
+
     if rank == 0:
         line = {
             "metric": f"dequant-GEMV weight GB/s ({args.fmt.upper()} {N}x{K}, B=1,2,4,8)",
@@ -459,12 +468,12 @@ def run_spiral(args):
                        "l2": f"inputs larger than L2: {copies} rotating weight copies "
                              f"({copies * shard_bytes / 2**20:.0f} MiB per rank > 126 MB L2)",
                        "parallelism": "single GPU" if world == 1 else
-                       f"row-shard x{world}, all-gather fused into the GEMV (NVLink peer stores + signal)",
+                       f"row-shard x{world}, all-gather fused into the GEMV (flagged NVLink stores)",
                        "graphs": f"CUDA graphs of {graph_steps} steps"},
             "roofline": roofline,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "note": "public C-ABI, pinned host x in / y out every step, weights resident"},
-            "gpu_launches": args.steps * len(BATCHES) * (1 if world == 1 else 2),
+            "gpu_launches": args.steps * len(BATCHES),
             "clocks": clk.summary(),
         }
         if cpu is not None:
@@ -477,7 +486,7 @@ def run_spiral(args):
 
     del main_cache
     if world > 1:
-        del po
+        del xc
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -100,8 +100,8 @@ SPIRAL_API const char* spiral_last_error(void);
 /* Synchronizes `stream`, then reads and clears the device-side error word of
  * the current device into *code.  Kernels never trap: a bounded wait (an
  * mbarrier or peer flag) that gives up sets a bit (1 = pipeline wait timeout,
- * 2 = tensor-memory allocation failure, 4 = bad launch geometry) and the
- * kernel ends early.  Returns SPIRAL_ERR_TIMEOUT when any bit was set.
+ * 2 = tensor-memory allocation failure, 4 = bad launch geometry, 8 = a
+ * rank's gathered-GEMV pieces never arrived) and the kernel ends early.  Returns SPIRAL_ERR_TIMEOUT when any bit was set.
  * No reference counterpart: the reference's only device watchdog is the XRT
  * run.wait2(5000 ms) host timeout (tests/poc/invoke.cc:25-26, 126-131). */
 SPIRAL_API int spiral_device_status(void* stream, uint32_t* code);
@@ -198,26 +198,31 @@ SPIRAL_API int spiral_mul_mat(int fmt, const void* w, int64_t w_row_stride_bytes
  * multi-device path — its multi-tile pattern splits weights by output column
  * and broadcasts the input, src/quants/tests/poc/calc.py:1-11, 154-215).
  * This rank computes y[m][n_offset + n] = sum_k bf16(Wshard[n][k]) x[m][k],
- * n < N_shard, m < M <= 8, and stores every bf16 output straight into the
- * full output of every rank (y_peers[r] + m * y_row_stride_elems +
- * n_offset + n, peer memory over NVLink); its last CTA then adds 1 to
- * signal_peers[r][rank] on every rank r and waits (bounded) for, and
- * consumes, one arrival from every rank, so the kernel completes only with
- * the whole gathered output in this rank's memory and work queued after it
- * on the stream sees all of it.
- * y_peers, signal_peers: DEVICE arrays of `world` device pointers (e.g. from
- * a symmetric-memory rendezvous); every y_peers[r] 16-byte aligned,
- * y_row_stride_elems and n_offset multiples of 8; each rank's signal block
- * holds world + 1 uint32, zero before the first call.  Every rank must make
- * the same calls in the same order.  A call can store into a peer's buffer
- * once that peer has finished the GEMV of its previous call, so two output
- * buffers used alternately are safe when every consumer of an output is
- * queued on the stream before the next call. */
+ * n < N_shard, m < M <= 8, into its full bf16 output y [M][N_total] (row
+ * stride y_row_stride_elems) and sends the same values to every other
+ * rank's exchange buffer over NVLink; it then copies the other ranks'
+ * columns from its own exchange buffer into y.  The kernel completes only
+ * with all N_total columns in y, so work queued after it on the stream sees
+ * the whole gathered output; y itself is never written by another rank.
+ * exchange_peers: DEVICE array of `world` device pointers, rank r's
+ * exchange buffer (spiral_allgather_exchange_bytes(N_total) bytes, 16-byte
+ * aligned, peer-mapped on every rank, e.g. by a symmetric-memory rendezvous,
+ * zeroed once before the first call).  Shards must be disjoint and cover
+ * [0, N_total); n_offset, N_shard, N_total and the row stride multiples of
+ * 8, y 16-byte aligned.  Every rank makes the same calls in the same order,
+ * with no other kernel running on its GPU meanwhile (the grid, one CTA per
+ * SM, must be co-resident), and calls on one exchange never overlap (one
+ * stream, or streams ordered by events).  A rank that does not arrive makes
+ * the others' bounded waits (2 s) give up with bit 8 of spiral_device_status;
+ * the ranks' call counts then disagree, so later calls skip their waits
+ * until the status is read, and the exchanges must be zeroed again on every
+ * rank before further use. */
+SPIRAL_API int64_t spiral_allgather_exchange_bytes(int64_t N_total);
 SPIRAL_API int spiral_mul_mat_allgather(int fmt, const void* w_shard, int64_t w_row_stride_bytes,
                                         const void* x, int64_t x_row_stride_elems,
-                                        void* const* y_peers, int64_t y_row_stride_elems,
-                                        int64_t n_offset, int64_t M, int64_t N_shard, int64_t K,
-                                        uint32_t* const* signal_peers, int rank, int world,
+                                        void* y, int64_t y_row_stride_elems, int64_t n_offset,
+                                        int64_t M, int64_t N_shard, int64_t N_total, int64_t K,
+                                        void* const* exchange_peers, int rank, int world,
                                         unsigned flags, void* stream);
 
 /* Fused unpack + mmul in the reference's tiled I/O orders:

@@ -44,8 +44,9 @@ _SIGNATURES = {
     "spiral_quants_unpack_all": ([_i32, _vp, _vp, _i64, _i64, _u32, _vp], _i32),
     "spiral_mul_mat": ([_i32, _vp, _i64, _vp, _i64, _vp, _i32, _i64, _i64, _i64, _i64, _u32, _vp], _i32),
     "spiral_quants_unpack_mmul_all": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _u32, _vp], _i32),
-    "spiral_mul_mat_allgather": ([_i32, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i32, _i32,
-                                  _u32, _vp], _i32),
+    "spiral_allgather_exchange_bytes": ([_i64], _i64),
+    "spiral_mul_mat_allgather": ([_i32, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i32,
+                                  _i32, _u32, _vp], _i32),
     "spiral_moe_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64], _i64),
     "spiral_moe_ffn": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i32,
                         _i64, _vp, _i64, _u32, _vp], _i32),
@@ -202,18 +203,29 @@ def unpack_mmul_all(fmt, packed, inputs_tiled, outputs, weights_rows: int, weigh
     return outputs
 
 
-def mul_mat_allgather(fmt, w_shard, x, N_shard: int, K: int, y_peers_dev, y_row_stride: int, n_offset: int,
-                      signal_peers_dev, rank: int, world: int, *, w_row_stride: int | None = None,
-                      ftz: bool = False, static_weights: bool = True, stream=None):
-    """Row-sharded MUL_MAT whose bf16 outputs land in every rank's full
-    output (peer stores) before the call's in-stream wait returns; see
-    spiral_b200.dist.PeerOutputs for the buffers."""
+def allgather_exchange_bytes(n_total: int) -> int:
+    """Bytes of one rank's exchange buffer for mul_mat_allgather (0 if
+    n_total is not a positive multiple of 8)."""
+    return int(lib().spiral_allgather_exchange_bytes(n_total))
+
+
+def mul_mat_allgather(fmt, w_shard, x, N_shard: int, K: int, y, n_offset: int, exchange_peers_dev, rank: int,
+                      world: int, *, w_row_stride: int | None = None, ftz: bool = False, static_weights: bool = True,
+                      stream=None):
+    """Row-sharded MUL_MAT with the all-gather fused in: y (bf16
+    [M][N_total], this rank's) receives every rank's shard; see
+    spiral_b200.dist.AllGatherExchange for the exchange buffers."""
+    import torch
+
     f = fmt_id(fmt)
-    M = int(x.shape[0])
+    M, n_total = int(x.shape[0]), int(y.shape[1])
+    if y.dtype != torch.bfloat16 or y.shape[0] < M:
+        raise ValueError("y must be bf16 with at least M rows")
     flags = (FLAG_FTZ_SCALES if ftz else 0) | (FLAG_STATIC_WEIGHTS if static_weights else 0)
     _check(lib().spiral_mul_mat_allgather(f, _ptr(w_shard), w_row_stride or row_bytes(f, K), _ptr(x),
-                                          int(x.stride(0)), _ptr(y_peers_dev), y_row_stride, n_offset, M, N_shard, K,
-                                          _ptr(signal_peers_dev), rank, world, flags, _stream(stream)))
+                                          int(x.stride(0)), _ptr(y), int(y.stride(0)), n_offset, M, N_shard,
+                                          n_total, K, _ptr(exchange_peers_dev), rank, world, flags,
+                                          _stream(stream)))
 
 
 # ---------------------------------------------------------------- MoE FFN

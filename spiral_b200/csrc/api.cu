@@ -294,25 +294,33 @@ int spiral_quants_unpack_mmul_all(int fmt, const void* packed, const void* input
   return run_mat(a, static_cast<cudaStream_t>(stream));
 }
 
+int64_t spiral_allgather_exchange_bytes(int64_t N_total) {
+  if (N_total <= 0 || (N_total & 7)) return 0;
+  return gemv_xchg_bytes(N_total);
+}
+
 int spiral_mul_mat_allgather(int fmt, const void* w_shard, int64_t w_row_stride_bytes, const void* x,
-                             int64_t x_row_stride_elems, void* const* y_peers, int64_t y_row_stride_elems,
-                             int64_t n_offset, int64_t M, int64_t N_shard, int64_t K, uint32_t* const* signal_peers,
+                             int64_t x_row_stride_elems, void* y, int64_t y_row_stride_elems, int64_t n_offset,
+                             int64_t M, int64_t N_shard, int64_t N_total, int64_t K, void* const* exchange_peers,
                              int rank, int world, unsigned flags, void* stream) {
   g_last_error[0] = 0;
   if (int st = check_shape(fmt, K, N_shard)) return st;
   if (M <= 0 || M > 8) return fail(SPIRAL_ERR_INVALID_SHAPE, "M=%lld: the gathered GEMV takes 1..8 vectors", (long long)M);
   if (world < 1 || world > 64 || rank < 0 || rank >= world)
     return fail(SPIRAL_ERR_INVALID_ARGUMENT, "rank %d / world %d", rank, world);
-  if (!w_shard || !x || !y_peers || !signal_peers) return fail(SPIRAL_ERR_NULL_POINTER, "null operand");
-  if (n_offset < 0 || y_row_stride_elems < n_offset + N_shard)
-    return fail(SPIRAL_ERR_INVALID_SHAPE, "shard columns [%lld, %lld) outside the output row of %lld",
-                (long long)n_offset, (long long)(n_offset + N_shard), (long long)y_row_stride_elems);
+  if (!w_shard || !x || !y || !exchange_peers) return fail(SPIRAL_ERR_NULL_POINTER, "null operand");
+  if (n_offset < 0 || N_total < n_offset + N_shard || y_row_stride_elems < N_total)
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "shard columns [%lld, %lld) outside the output of %lld (row stride %lld)",
+                (long long)n_offset, (long long)(n_offset + N_shard), (long long)N_total,
+                (long long)y_row_stride_elems);
   if (w_row_stride_bytes < row_bytes(fmt, K) || x_row_stride_elems < K)
     return fail(SPIRAL_ERR_INVALID_SHAPE, "w/x row strides smaller than a row");
   if ((reinterpret_cast<uintptr_t>(w_shard) & 15u) || (w_row_stride_bytes & 15) || (reinterpret_cast<uintptr_t>(x) & 1u))
     return fail(SPIRAL_ERR_ALIGNMENT, "weights need 16-byte aligned rows");
-  if ((y_row_stride_elems & 7) || (n_offset & 7))
-    return fail(SPIRAL_ERR_ALIGNMENT, "output row stride and shard offset must be multiples of 8 elements");
+  if ((reinterpret_cast<uintptr_t>(y) & 15u) || (y_row_stride_elems & 7) || (n_offset & 7) || (N_shard & 7) ||
+      (N_total & 7))
+    return fail(SPIRAL_ERR_ALIGNMENT,
+                "gathered output: 16-byte aligned, row stride, shard offset, shard and total multiples of 8");
   MatArgs a{};
   a.fmt = fmt;
   a.w = static_cast<const uint8_t*>(w_shard);
@@ -320,7 +328,7 @@ int spiral_mul_mat_allgather(int fmt, const void* w_shard, int64_t w_row_stride_
   a.x = static_cast<const uint16_t*>(x);
   a.x_s8 = 8;
   a.x_sm = x_row_stride_elems;
-  a.y = nullptr;
+  a.y = y;
   a.y_s8 = 8;
   a.y_sm = y_row_stride_elems;
   a.y_bf16 = true;
@@ -329,7 +337,7 @@ int spiral_mul_mat_allgather(int fmt, const void* w_shard, int64_t w_row_stride_
   a.M = M;
   a.N = N_shard;
   a.K = K;
-  PeerOut po{y_peers, signal_peers, n_offset, rank, world};
+  PeerOut po{reinterpret_cast<uint8_t* const*>(exchange_peers), n_offset, N_total, rank, world};
   const cudaError_t e = gemv_allgather(a, po, static_cast<cudaStream_t>(stream));
   if (e == cudaErrorNotSupported)
     return fail(SPIRAL_ERR_UNSUPPORTED, "shape not served by the pipelined GEMV (K=%lld)", (long long)K);

@@ -41,16 +41,16 @@ struct MatArgs {
 bool gemv_fast_ok(const MatArgs& a);
 cudaError_t gemv(const MatArgs& a, cudaStream_t stream);
 
-// Row-sharded GEMV whose epilogue stores into every rank's full output
-// (peer memory over NVLink) and signals; then an in-stream bounded wait for
-// every rank's shard.  y_peers / sig_peers are device arrays of `world`
-// pointers; each rank's signal words hold world + 1 uint32, zero at start.
+// Row-sharded GEMV with the all-gather fused in (gemv.cu): a.y is this
+// rank's full bf16 output [M][a.y_sm]; the shard's rows are its columns
+// [n_offset, n_offset + a.N); xchg_peers is a device array of `world`
+// exchange buffers (gemv_xchg_bytes(n_total) each, zeroed before first use).
 struct PeerOut {
-  void* const* y_peers;
-  uint32_t* const* sig_peers;
-  int64_t n_offset;
+  uint8_t* const* xchg_peers;
+  int64_t n_offset, n_total;
   int rank, world;
 };
+int64_t gemv_xchg_bytes(int64_t n_total);
 cudaError_t gemv_allgather(const MatArgs& a, const PeerOut& po, cudaStream_t stream);
 
 // gemm.cu — tcgen05 dequant-GEMM for larger M.

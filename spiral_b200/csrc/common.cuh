@@ -34,6 +34,7 @@ enum : uint32_t {
   kDevErrMbarTimeout = 1u << 0,
   kDevErrTmemAlloc = 1u << 1,
   kDevErrBadLaunch = 1u << 2,
+  kDevErrPeerTimeout = 1u << 3,  // a rank's gathered-GEMV pieces never arrived
 };
 extern __device__ uint32_t g_device_error;
 

@@ -72,15 +72,33 @@ struct GemvParams {
   int x_pitch;    // bytes per activation vector in the permuted copy
   int y_bf16, accumulate, ftz;
   int static_weights;  // weights may be read before the preceding grid ends
-  // Peer output (world > 0): every output goes to column n_offset + n of
-  // each rank's full output (y_peers[r], bf16, row stride y_sm); the last CTA
-  // then raises this rank's counter on every rank (sig_peers[r][rank]) and
-  // consumes one arrival of every rank from its own counters.
-  void* const* y_peers;
-  uint32_t* const* sig_peers;
-  int64_t n_offset;
+  // Gathered output (world > 0): y is this rank's full bf16 output
+  // [M][y_sm]; the shard's rows are columns n_offset + n of it, and every
+  // rank's exchange buffer (xchg_peers[r]) receives them as flagged units.
+  uint8_t* const* xchg_peers;
+  int64_t n_offset, n_total;
   int rank, world;
 };
+
+// Exchange buffer of the gathered GEMV (one per rank, peer-mapped): a
+// 256-byte control block (word 0: calls completed on this rank, word 1: CTA
+// count of the running call) and two slots (call parity) of [8][n_total / 2]
+// units.  A unit is 8 bytes, two bf16 outputs (columns 2u, 2u + 1) in the
+// low word and the call's flag in the high word, stored and loaded as one
+// 64-bit access, so a reader that sees the flag sees the data: no fence is
+// needed on either side.  Units travel in 16-byte pairs (4 columns).
+constexpr int64_t kXchgCtrlBytes = 256;
+__host__ __device__ constexpr int64_t xchg_slot_bytes(int64_t n_total) { return 8 * n_total * 4; }
+
+__device__ __forceinline__ uint32_t xchg_flag(uint32_t calls) { return calls | 0x80000000u; }
+
+__device__ __forceinline__ void st_pair_sys(uint8_t* dst, uint64_t a, uint64_t b) {
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(a), "l"(b) : "memory");
+}
+
+__device__ __forceinline__ void ld_pair_sys(const uint8_t* src, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(src) : "memory");
+}
 
 // ------------------------------------------------- activation staging ----
 
@@ -218,6 +236,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
 
   // --------------------------------------------------------- consumers -----
   griddep_wait();  // activations may come from the preceding kernel
+  // calls completed on this rank: the parity and flag of this gathered call
+  const uint32_t calls = p.world > 0 ? *reinterpret_cast<volatile const uint32_t*>(p.xchg_peers[p.rank]) : 0u;
   stage_x<FMT>(p, xs, reinterpret_cast<uint8_t*>(red), threadIdx.x);
   named_bar_sync(kGroupsPerCta + 1, kConsumerWarps * 32);
 
@@ -270,24 +290,36 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
       const int m = 2 * (l & 3) + (j & 1);
       const int64_t n = tile * kTileRows + row;
       if (p.world > 0) {
-        // Peer output: the tile's bf16 outputs are gathered in shared memory
-        // (the reduction slots, free once every sum is read) as [m][16 rows],
-        // then leave in 16-byte pieces, one per (rank, m, half-tile).
+        // Gathered output: the tile's bf16 outputs are collected in shared
+        // memory (the reduction slots, free once every sum is read) as
+        // [m][16 rows]; 16-byte pieces then go to the local output and, as
+        // flagged unit pairs, to every other rank's exchange slot.  Shards
+        // are multiples of 8 rows, so a piece is either whole or absent.
         uint16_t* tile_out = reinterpret_cast<uint16_t*>(gred);
         named_bar_sync(kGroupsPerCta + 2 + grp, 128);
         tile_out[m * kTileRows + row] = static_cast<uint16_t>(pack_bf16x2(sum, 0.f) & 0xFFFFu);
         named_bar_sync(kGroupsPerCta + 2 + grp, 128);
-        const int items = p.M * 2 * p.world;
+        const int64_t r0 = tile * kTileRows;
+        const int local_items = p.M * 2;
+        const int items = *(volatile int*)&abort_flag ? local_items : local_items + p.M * 4 * (p.world - 1);
         for (int it = t; it < items; it += 128) {
-          const int half = it & 1, mm = (it >> 1) % p.M, rr = (it >> 1) / p.M;
-          const int64_t n0 = tile * kTileRows + half * 8;
-          if (n0 >= p.N) continue;
-          uint16_t* dst = static_cast<uint16_t*>(p.y_peers[rr]) + static_cast<int64_t>(mm) * p.y_sm + p.n_offset + n0;
-          const uint16_t* src = tile_out + mm * kTileRows + half * 8;
-          if (n0 + 8 <= p.N) {
-            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+          if (it < local_items) {
+            const int half = it & 1, mm = it >> 1;
+            if (r0 + half * 8 + 8 > p.N) continue;
+            *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + static_cast<int64_t>(mm) * p.y_sm + p.n_offset +
+                                      r0 + half * 8) =
+                *reinterpret_cast<const uint4*>(tile_out + mm * kTileRows + half * 8);
           } else {
-            for (int e = 0; e < p.N - n0; ++e) dst[e] = src[e];
+            const int q = it - local_items;
+            const int piece = q & 3, mm = (q >> 2) % p.M, k = (q >> 2) / p.M;
+            if (r0 + piece * 4 + 4 > p.N) continue;
+            const int rr = k < p.rank ? k : k + 1;
+            const uint2 d = *reinterpret_cast<const uint2*>(tile_out + mm * kTileRows + piece * 4);
+            const uint64_t hi = static_cast<uint64_t>(xchg_flag(calls)) << 32;
+            const int64_t col = p.n_offset + r0 + piece * 4;
+            st_pair_sys(p.xchg_peers[rr] + kXchgCtrlBytes + (calls & 1) * xchg_slot_bytes(p.n_total) +
+                            mm * 4 * p.n_total + col * 4,
+                        hi | d.x, hi | d.y);
           }
         }
       } else if (m < p.M && n < p.N) {
@@ -304,46 +336,52 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     named_bar_sync(1 + grp, kWarpsPerGroup * 32);
   }
   if (p.world > 0) {
-    // Every output of this CTA is stored (to all ranks) before it counts
-    // itself done.  The CTA that completes the count tells every rank, after
-    // a system-scope fence, that this rank's shard has landed, then waits
-    // (bounded) for one arrival from every rank and consumes it: the grid
-    // completes only once the whole output is in this rank's memory, so
-    // stream order alone covers every later reader.  Each rank signals
-    // before it waits, so the waits cannot cycle.  A CTA whose pipeline gave
-    // up marks the count (bit 31) and no rank is signalled: their bounded
-    // waits then report the failure instead of passing on a partial shard.
-    // The next call's CTAs add to the count only after this grid completed
-    // (their consumers wait for it), so the reset below is never raced.
+    // Receive: the grid's consumer threads poll the other ranks' pieces of
+    // the output in this rank's exchange slot (bounded) and copy them to the
+    // local output; the grid completes only once the whole gathered output
+    // is local, so stream order alone covers every later reader.  Every CTA
+    // has sent all its pieces before it polls, and the grid (one CTA per SM)
+    // is co-resident, so the waits cannot cycle.
+    const int64_t pieces_per_row = p.n_total / 4;
+    const int64_t total = static_cast<int64_t>(p.M) * pieces_per_row;
+    const uint8_t* slot = p.xchg_peers[p.rank] + kXchgCtrlBytes + (calls & 1) * xchg_slot_bytes(p.n_total);
+    const uint32_t flag = xchg_flag(calls);
+    // After a rank failed to arrive the ranks' call counts no longer agree:
+    // later calls skip their waits (the error stays set until the host reads
+    // it) instead of each waiting out the limit.
+    bool ok = !*(volatile int*)&abort_flag && !(*(volatile uint32_t*)&g_device_error & kDevErrPeerTimeout);
+    for (int64_t q = static_cast<int64_t>(blockIdx.x) * kStageThreads + threadIdx.x; ok && q < total;
+         q += static_cast<int64_t>(gridDim.x) * kStageThreads) {
+      const int64_t mm = q / pieces_per_row, col = (q - mm * pieces_per_row) * 4;
+      if (col >= p.n_offset && col < p.n_offset + p.N) continue;
+      const uint8_t* src = slot + mm * 4 * p.n_total + col * 4;
+      uint64_t a, b;
+      const uint64_t t0 = globaltimer_ns();
+      for (;;) {
+        ld_pair_sys(src, a, b);
+        if (static_cast<uint32_t>(a >> 32) == flag && static_cast<uint32_t>(b >> 32) == flag) break;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          raise_device_error(kDevErrPeerTimeout);
+          ok = false;
+          break;
+        }
+      }
+      if (ok) {
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.y) + mm * p.y_sm + col) =
+            make_uint2(static_cast<uint32_t>(a), static_cast<uint32_t>(b));
+      }
+    }
+    // The last CTA to finish advances the call count (the parity and flag of
+    // the next call); every CTA read it before adding itself here, and the
+    // next call's CTAs read it only after this grid has completed.
     named_bar_sync(kGroupsPerCta + 1, kConsumerWarps * 32);
     if (threadIdx.x == 0) {
-      __threadfence_system();  // cumulative: covers the CTA's stores ordered before the barrier
-      uint32_t* mine = p.sig_peers[p.rank];
-      uint32_t* done = mine + p.world;
-      if (*(volatile int*)&abort_flag) atomicOr(done, 0x80000000u);
-      const uint32_t before = atomicAdd(done, 1u);
-      if ((before & 0x7FFFFFFFu) == gridDim.x - 1) {
-        *done = 0u;
-        __threadfence_system();
-        if (!(before & 0x80000000u)) {
-          for (int rr = 0; rr < p.world; ++rr) atomicAdd_system(p.sig_peers[rr] + p.rank, 1u);
-        }
-        for (int rr = 0; rr < p.world; ++rr) {
-          const uint64_t t0 = globaltimer_ns();
-          bool arrived = true;
-          for (;;) {
-            uint32_t v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + rr) : "memory");
-            if (v >= 1u) break;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-              raise_device_error(kDevErrMbarTimeout);
-              arrived = false;
-              break;
-            }
-          }
-          if (!arrived) break;
-          atomicSub(mine + rr, 1u);
-        }
+      uint32_t* ctrl = reinterpret_cast<uint32_t*>(p.xchg_peers[p.rank]);
+      uint32_t before;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(before) : "l"(ctrl + 1) : "memory");
+      if (before == gridDim.x - 1) {
+        ctrl[1] = 0u;
+        ctrl[0] = calls + 1u;
       }
     }
   }
@@ -487,9 +525,9 @@ static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream, const PeerOut* 
   p.ftz = a.ftz;
   p.static_weights = a.static_weights;
   if (po != nullptr) {
-    p.y_peers = po->y_peers;
-    p.sig_peers = po->sig_peers;
+    p.xchg_peers = po->xchg_peers;
     p.n_offset = po->n_offset;
+    p.n_total = po->n_total;
     p.rank = po->rank;
     p.world = po->world;
   }
@@ -528,6 +566,8 @@ cudaError_t gemv(const MatArgs& a, cudaStream_t stream) {
   }
   return cudaErrorInvalidValue;
 }
+
+int64_t gemv_xchg_bytes(int64_t n_total) { return kXchgCtrlBytes + 2 * xchg_slot_bytes(n_total); }
 
 cudaError_t gemv_allgather(const MatArgs& a, const PeerOut& po, cudaStream_t stream) {
   switch (a.fmt) {

@@ -104,32 +104,27 @@ def moe_dispatch_combine(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tens
     return y
 
 
-class PeerOutputs:
-    """Full-size bf16 output buffers that every rank can store into, for
-    spiral_b200.mul_mat_allgather: one symmetric-memory allocation per rank
-    (torch.distributed._symmetric_memory, peer-mapped over NVLink) holding an
-    [M][N] bf16 output per key plus the signal words, and device arrays of the
-    peers' pointers.  Collective: every rank constructs it with the same
-    shapes."""
+class AllGatherExchange:
+    """Exchange buffers for spiral_b200.mul_mat_allgather over a gathered
+    width of n_total columns: one symmetric-memory allocation per rank
+    (torch.distributed._symmetric_memory, peer-mapped over NVLink), zeroed,
+    and the device array of every rank's pointer (``peers``).  Collective:
+    every rank constructs it with the same n_total.  One exchange serves any
+    number of calls (and outputs) of that width issued in the same order on
+    every rank."""
 
-    def __init__(self, shapes: dict, device, group=None):
+    def __init__(self, n_total: int, device, group=None):
         import torch.distributed._symmetric_memory as symm_mem
 
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
-        offs, off = {}, 0
-        for key, (m, n) in shapes.items():
-            offs[key] = off
-            off += ((m * n * 2 + 255) // 256) * 256
-        sig_off = off
-        total = sig_off + 256 * ((4 * (self.world + 1) + 255) // 256)
-        self._buf = symm_mem.empty(total, dtype=torch.uint8, device=device)
+        from . import allgather_exchange_bytes
+
+        nbytes = allgather_exchange_bytes(n_total)
+        if nbytes <= 0:
+            raise ValueError("n_total must be a positive multiple of 8")
+        self.n_total = n_total
+        self._buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
         self._buf.zero_()
         self._hdl = symm_mem.rendezvous(self._buf, group=group if group is not None else dist.group.WORLD)
-        ptrs = list(self._hdl.buffer_ptrs)
-        self.signals = torch.tensor([p + sig_off for p in ptrs], dtype=torch.int64, device=device)
-        self.y_peers, self.y = {}, {}
-        for key, (m, n) in shapes.items():
-            self.y_peers[key] = torch.tensor([p + offs[key] for p in ptrs], dtype=torch.int64, device=device)
-            self.y[key] = self._buf[offs[key]:offs[key] + m * n * 2].view(torch.bfloat16).view(m, n)
+        self.peers = torch.tensor(list(self._hdl.buffer_ptrs), dtype=torch.int64, device=device)
+        torch.cuda.synchronize(device)
         dist.barrier(group=group)

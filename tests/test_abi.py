@@ -167,13 +167,17 @@ def test_moe_validation_codes():
 
 def test_mul_mat_allgather_validation_codes():
     L = sp.lib()
+    assert sp.allgather_exchange_bytes(14336) == 256 + 2 * 32 * 14336
+    assert sp.allgather_exchange_bytes(14332) == 0
+    assert sp.allgather_exchange_bytes(0) == 0
 
     def call(**kw):
-        a = dict(fmt=sp.Q4_0, w=256, ws=2304, x=256, xs=4096, yp=256, ys=14336, off=7168, M=8, N=7168, K=4096,
-                 sig=256, rank=1, world=2, flags=0)
+        a = dict(fmt=sp.Q4_0, w=256, ws=2304, x=256, xs=4096, y=256, ys=14336, off=7168, M=8, N=7168, NT=14336,
+                 K=4096, xc=256, rank=1, world=2, flags=0)
         a.update(kw)
-        return L.spiral_mul_mat_allgather(a["fmt"], a["w"], a["ws"], a["x"], a["xs"], a["yp"], a["ys"], a["off"],
-                                          a["M"], a["N"], a["K"], a["sig"], a["rank"], a["world"], a["flags"], 0)
+        return L.spiral_mul_mat_allgather(a["fmt"], a["w"], a["ws"], a["x"], a["xs"], a["y"], a["ys"], a["off"],
+                                          a["M"], a["N"], a["NT"], a["K"], a["xc"], a["rank"], a["world"],
+                                          a["flags"], 0)
 
     assert call(fmt=3) == -1
     assert call(K=4001) == -2
@@ -181,11 +185,13 @@ def test_mul_mat_allgather_validation_codes():
     assert call(M=0) == -2
     assert call(rank=2) == -10
     assert call(world=0) == -10
-    assert call(yp=0) == -3
-    assert call(sig=0) == -3
-    assert call(off=7169) == -2  # shard runs past the output row
-    assert call(off=-1) == -2
+    assert call(y=0) == -3
+    assert call(xc=0) == -3
+    assert call(off=7176) == -2  # shard runs past the gathered width
+    assert call(off=-8) == -2
+    assert call(ys=14328) == -2  # row stride below the gathered width
     assert call(ws=2000) == -2
     assert call(w=264) == -4
-    assert call(off=4) == -4  # 16-byte output pieces
+    assert call(off=7164, N=7172) == -4  # 8-column granularity
     assert call(ys=14340) == -4
+    assert call(y=264) == -4

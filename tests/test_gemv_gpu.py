@@ -225,42 +225,47 @@ def test_gemv_unaligned_activations_and_long_k(cuda, fid, M, N, K, x_off):
 
 @pytest.mark.parametrize("fid", FMTS, ids=lambda f: F.NAMES[f])
 def test_gathered_gemv_single_rank(cuda, fid):
-    """spiral_mul_mat_allgather with world = 1 on one GPU: the shard lands at
-    its column offset of the full output row, the signal/wait pair counts one
-    arrival per call (the done counter resets), eagerly and in a replayed CUDA
-    graph.  The peer stores and signals on 2 GPUs are covered by
+    """spiral_mul_mat_allgather with world = 1 on one GPU (the one shard is
+    the whole width): outputs land in a strided row, the padding after the
+    gathered width is left alone, the call count advances once per call (the
+    exchange slots alternate), eagerly and in a replayed CUDA graph.  Shard
+    offsets and the exchange between ranks are covered on 2 GPUs by
     test_multi_gpu."""
     import torch
 
-    K, N, Nfull, off = 4096, 1808, 2048, 224
+    K, N, stride, off = 4096, 1800, 2048, 0  # 1800 rows: a ragged last tile of 8
     raw = F.generate(fid, K, N, seed=31)
     w = dev_bytes(raw)
-    y = torch.zeros((8, Nfull), dtype=torch.bfloat16, device="cuda")
-    sig = torch.zeros(64, dtype=torch.int32, device="cuda")
-    y_peers = torch.tensor([y.data_ptr()], dtype=torch.int64, device="cuda")
-    sig_peers = torch.tensor([sig.data_ptr()], dtype=torch.int64, device="cuda")
+    y_rows = torch.zeros((8, stride), dtype=torch.bfloat16, device="cuda")
+    y = y_rows[:, :N]
+    xchg = torch.zeros(sp.allgather_exchange_bytes(N), dtype=torch.uint8, device="cuda")
+    peers = torch.tensor([xchg.data_ptr()], dtype=torch.int64, device="cuda")
+    calls = 0
     for it, M in enumerate((1, 3, 8, 8)):
         x = F.gen_activations(M, K, seed=40 + it)
-        sp.mul_mat_allgather(fid, w, dev_bf16(x), N, K, y_peers, Nfull, off, sig_peers, 0, 1)
-        got = y[:M].float().cpu().numpy()
+        sp.mul_mat_allgather(fid, w, dev_bf16(x), N, K, y, off, peers, 0, 1)
+        calls += 1
+        got = y_rows[:M].float().cpu().numpy()
         ok, rel = tolerance_ok(got[:, off:off + N], oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=True)
         assert ok, (M, rel)
-        assert not got[:, :off].any() and not got[:, off + N:].any()
-    assert sig.cpu().tolist()[:2] == [0, 0]
+        assert not got[:, off + N:].any()
+    ctrl = xchg[:8].view(torch.int32).cpu().tolist()
+    assert ctrl == [calls, 0]
 
     x = F.gen_activations(4, K, seed=50)
     xd = dev_bf16(x)
     s = torch.cuda.Stream()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=s):
-        sp.mul_mat_allgather(fid, w, xd, N, K, y_peers, Nfull, off, sig_peers, 0, 1, stream=s)
-    y.zero_()
+        sp.mul_mat_allgather(fid, w, xd, N, K, y, off, peers, 0, 1, stream=s)
+    y_rows.zero_()
     for _ in range(3):
         g.replay()
     torch.cuda.synchronize()
-    ok, rel = tolerance_ok(y[:4, off:off + N].float().cpu().numpy(), oracle.mul_mat_f64(fid, raw, x, K, N),
+    calls += 3
+    ok, rel = tolerance_ok(y_rows[:4, off:off + N].float().cpu().numpy(), oracle.mul_mat_f64(fid, raw, x, K, N),
                            bf16_out=True)
     assert ok, rel
     del g
-    assert sig.cpu().tolist()[:2] == [0, 0]
+    assert xchg[:8].view(torch.int32).cpu().tolist() == [calls, 0]
     assert sp.device_status() == 0

@@ -57,29 +57,30 @@ def _worker(rank, world, port, q):
         y = gather_rows(y_local, N).cpu().numpy()
         ok_dense, rel_dense = tolerance_ok(y, oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=False)
 
-        # the same GEMV with the all-gather fused in (peer stores + signals),
-        # uneven shards (113 tiles of 16 rows over 2 ranks), every batch size,
-        # two buffers used alternately, several calls in a row
-        from spiral_b200.dist import PeerOutputs
+        # the same GEMV with the all-gather fused in (flagged units over
+        # NVLink), uneven shards (113 tiles of 16 rows over 2 ranks), every
+        # batch size, one output per batch size, several calls in a row
+        # through one exchange
+        from spiral_b200.dist import AllGatherExchange
 
         Ng = 1808
         rawg = F.generate(fid, K, Ng, seed=7)
         g0, g1 = row_range(Ng, world, rank)
         wg_shard = torch.from_numpy(rawg[g0 * rb:g1 * rb]).to(dev)
-        po = PeerOutputs({(B, s): (B, Ng) for B in (1, 2, 5, 8) for s in (0, 1)}, dev)
+        xc = AllGatherExchange(Ng, dev)
+        outs = {B: torch.zeros((B, Ng), dtype=torch.bfloat16, device=dev) for B in (1, 2, 5, 8)}
         ok_fused, rel_fused = True, 0.0
-        for it in range(6):
+        for it in range(7):
             B = (1, 2, 5, 8)[it % 4]
             xb = F.gen_activations(B, K, seed=20 + it)
             xdb = torch.from_numpy(xb.view(np.int16)).to(dev).view(torch.bfloat16)
-            sp.mul_mat_allgather(fid, wg_shard, xdb, g1 - g0, K, po.y_peers[(B, it % 2)], Ng, g0, po.signals, rank,
-                                 world)
-            yg = po.y[(B, it % 2)].float().cpu().numpy()
+            sp.mul_mat_allgather(fid, wg_shard, xdb, g1 - g0, K, outs[B], g0, xc.peers, rank, world)
+            yg = outs[B].float().cpu().numpy()
             ok, rel = tolerance_ok(yg, oracle.mul_mat_f64(fid, rawg, xb, K, Ng), bf16_out=True)
             ok_fused, rel_fused = ok_fused and ok, max(rel_fused, rel)
         torch.cuda.synchronize()
         dist.barrier()
-        del po
+        del xc
 
         # MoE: 16 Q4_0 experts, hidden 512, inter 256, top-4, tokens sharded
         E, H, I, T, topk = 16, 512, 256, 9, 4
