@@ -172,7 +172,9 @@ __device__ void stage_x(const GemvParams& p, uint8_t* xs, uint8_t* raw, int tid)
 
 // --------------------------------------------------------------- kernel ---
 
-template <int FMT>
+// GATHER: the row-sharded call with the all-gather fused in (p.world > 0);
+// a separate instantiation so the plain GEMV carries none of its code.
+template <int FMT, bool GATHER>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams p) {
   using F = GemvFmt<FMT>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -237,7 +239,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
   // --------------------------------------------------------- consumers -----
   griddep_wait();  // activations may come from the preceding kernel
   // calls completed on this rank: the parity and flag of this gathered call
-  const uint32_t calls = p.world > 0 ? *reinterpret_cast<volatile const uint32_t*>(p.xchg_peers[p.rank]) : 0u;
+  uint32_t calls = 0u;
+  if constexpr (GATHER) calls = *reinterpret_cast<volatile const uint32_t*>(p.xchg_peers[p.rank]);
   stage_x<FMT>(p, xs, reinterpret_cast<uint8_t*>(red), threadIdx.x);
   named_bar_sync(kGroupsPerCta + 1, kConsumerWarps * 32);
 
@@ -289,7 +292,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
       const int row = (l >> 2) + 8 * (j >> 1);
       const int m = 2 * (l & 3) + (j & 1);
       const int64_t n = tile * kTileRows + row;
-      if (p.world > 0) {
+      if constexpr (GATHER) {
         // Gathered output: the tile's bf16 outputs are collected in shared
         // memory (the reduction slots, free once every sum is read) as
         // [m][16 rows]; 16-byte pieces then go to the local output and, as
@@ -335,7 +338,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     }
     named_bar_sync(1 + grp, kWarpsPerGroup * 32);
   }
-  if (p.world > 0) {
+  if constexpr (GATHER) {
     // Receive: the grid's consumer threads poll the other ranks' pieces of
     // the output in this rank's exchange slot (bounded) and copy them to the
     // local output; the grid completes only once the whole gathered output
@@ -534,10 +537,11 @@ static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream, const PeerOut* 
 
   int dev = 0;
   cudaGetDevice(&dev);
-  const int slot = FMT == kQ4_0 ? 0 : (FMT == kQ8_0 ? 1 : 2);
-  static std::atomic<bool> configured[64][3];
+  const int slot = (FMT == kQ4_0 ? 0 : (FMT == kQ8_0 ? 1 : 2)) + (po != nullptr ? 3 : 0);
+  static std::atomic<bool> configured[64][6];
+  auto* kernel = po != nullptr ? gemv_kernel<FMT, true> : gemv_kernel<FMT, false>;
   if (!configured[dev & 63][slot].load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(device_max_smem_optin()));
     if (e != cudaSuccess) return e;
     configured[dev & 63][slot].store(true, std::memory_order_release);
@@ -555,7 +559,7 @@ static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream, const PeerOut* 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_kernel<FMT>, p);
+  return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
 cudaError_t gemv(const MatArgs& a, cudaStream_t stream) {
