@@ -174,7 +174,9 @@ __device__ void stage_x(const GemvParams& p, uint8_t* xs, uint8_t* raw, int tid)
 
 // GATHER: the row-sharded call with the all-gather fused in (p.world > 0);
 // a separate instantiation so the plain GEMV carries none of its code.
-template <int FMT, bool GATHER>
+// FTZ: the flush of subnormal scales, fixed at compile time so the decode
+// loop carries no test for it (p.ftz is not read).
+template <int FMT, bool GATHER, bool FTZ>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams p) {
   using F = GemvFmt<FMT>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -268,15 +270,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         const uint8_t* st = stages + s * stage_bytes;
         const uint8_t* ra = st + r * p.row_pitch;
         const uint8_t* rb = st + (r + 8) * p.row_pitch;
-        for (int gl = gw; gl < ng; gl += kWarpsPerGroup) {
+        auto decode = [&](int gl) {
           const uint8_t* xg = xcol + (g0 + gl) * F::kSteps * 32;
           if constexpr (FMT == kQ6_K) {
-            GroupDecoder<FMT>::run(ra + gl * F::kGroupBytes, rb + gl * F::kGroupBytes, c, xg, p.ftz != 0, acc,
+            GroupDecoder<FMT>::run(ra + gl * F::kGroupBytes, rb + gl * F::kGroupBytes, c, xg, FTZ, acc,
                                    (gl & 1) ? 16u : 0u);
           } else {
-            GroupDecoder<FMT>::run(ra + gl * F::kGroupBytes, rb + gl * F::kGroupBytes, c, xg, p.ftz != 0, acc);
+            GroupDecoder<FMT>::run(ra + gl * F::kGroupBytes, rb + gl * F::kGroupBytes, c, xg, FTZ, acc);
           }
+        };
+        // groups gw, gw + 8, ... < ng, two per iteration so the second
+        // group's decode overlaps the first one's MMAs
+        int gl = gw;
+        for (; gl + kWarpsPerGroup < ng; gl += 2 * kWarpsPerGroup) {
+          decode(gl);
+          decode(gl + kWarpsPerGroup);
         }
+        if (gl < ng) decode(gl);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -537,9 +547,10 @@ static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream, const PeerOut* 
 
   int dev = 0;
   cudaGetDevice(&dev);
-  const int slot = (FMT == kQ4_0 ? 0 : (FMT == kQ8_0 ? 1 : 2)) + (po != nullptr ? 3 : 0);
-  static std::atomic<bool> configured[64][6];
-  auto* kernel = po != nullptr ? gemv_kernel<FMT, true> : gemv_kernel<FMT, false>;
+  const int slot = (FMT == kQ4_0 ? 0 : (FMT == kQ8_0 ? 1 : 2)) + (po != nullptr ? 3 : 0) + (a.ftz ? 6 : 0);
+  static std::atomic<bool> configured[64][12];
+  auto* kernel = po != nullptr ? (a.ftz ? gemv_kernel<FMT, true, true> : gemv_kernel<FMT, true, false>)
+                               : (a.ftz ? gemv_kernel<FMT, false, true> : gemv_kernel<FMT, false, false>);
   if (!configured[dev & 63][slot].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(device_max_smem_optin()));
