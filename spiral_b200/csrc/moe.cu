@@ -272,32 +272,41 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_gemv(const MoeArgs a, int 
 
   if (warp == kMoeConsumers) {
     // ------------------------------------------------------- producer ----
-    if (lane == 0) {
-      const uint64_t pol = l2_evict_first_policy();
-      const uint32_t bytes = static_cast<uint32_t>(rb);
-      uint32_t it = 0;
-      for (int64_t i = i_begin; i < i_end; ++i, ++it) {
-        const MoeProblem pr = probs[i / tiles];
-        const int tile = static_cast<int>(i % tiles);
-        const int s = static_cast<int>(it % stages);
-        if (!mbar_wait(&empty[s], ((it / stages) & 1u) ^ 1u) || *(volatile int*)&abort_flag) {
-          abort_flag = 1;
-          break;
-        }
-        mbar_arrive_expect_tx(&full[s], bytes * P::kRows);
-        uint8_t* dst = stg + s * stage_bytes;
-        const int64_t row0 = static_cast<int64_t>(pr.expert) * N + tile * kTileRows;
-        if constexpr (PHASE == 1) {
-          for (int r = 0; r < kTileRows; ++r) {
-            bulk_g2s(dst + r * row_pitch, a.w_gate + (row0 + r) * rb, bytes, &full[s], pol);
-            bulk_g2s(dst + (kTileRows + r) * row_pitch, a.w_up + (row0 + r) * rb, bytes, &full[s], pol);
-          }
+    // Lane 0 waits for a free stage and posts the byte count; then lane l
+    // (< kRows) issues the copy of stage row l, so an item's 16 or 32 row
+    // copies leave in one instruction (items are small: one thread issuing
+    // them one by one would pace the down projection).
+    const uint64_t pol = l2_evict_first_policy();
+    const uint32_t bytes = static_cast<uint32_t>(rb);
+    uint32_t it = 0;
+    for (int64_t i = i_begin; i < i_end; ++i, ++it) {
+      const MoeProblem pr = probs[i / tiles];
+      const int tile = static_cast<int>(i % tiles);
+      const int s = static_cast<int>(it % stages);
+      int go = 0;
+      if (lane == 0) {
+        go = mbar_wait(&empty[s], ((it / stages) & 1u) ^ 1u) && !*(volatile int*)&abort_flag;
+        if (go) {
+          mbar_arrive_expect_tx(&full[s], bytes * P::kRows);
         } else {
-          for (int r = 0; r < kTileRows; ++r)
-            bulk_g2s(dst + r * row_pitch, a.w_down + (row0 + r) * rb, bytes, &full[s], pol);
+          abort_flag = 1;
         }
       }
-      // Every issued stage must land before the CTA may exit.
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+      if (lane < P::kRows) {
+        uint8_t* dst = stg + s * stage_bytes + lane * row_pitch;
+        const int64_t row0 = static_cast<int64_t>(pr.expert) * N + tile * kTileRows;
+        const uint8_t* src;
+        if constexpr (PHASE == 1) {
+          src = lane < kTileRows ? a.w_gate + (row0 + lane) * rb : a.w_up + (row0 + lane - kTileRows) * rb;
+        } else {
+          src = a.w_down + (row0 + lane) * rb;
+        }
+        bulk_g2s(dst, src, bytes, &full[s], pol);
+      }
+    }
+    // Every issued stage must land before the CTA may exit.
+    if (lane == 0) {
       const uint32_t first = it > static_cast<uint32_t>(stages) ? it - stages : 0u;
       for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % stages], (j / stages) & 1u);
     }
