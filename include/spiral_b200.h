@@ -285,9 +285,14 @@ SPIRAL_API int spiral_moe_ffn(int fmt, const void* w_gate, const void* w_up, con
  * with SPIRAL_ERR_CAPACITY (config-4 dims, 128 experts x hidden 2048 x inter
  * 768 at top-8, fit up to 107 tokens).  The first call on a device looks up
  * the array's device address; make that first call before any stream
- * capture.  All calls share the array: calls that overlap on the GPU race on
- * it, so order them (one stream, or events).  Arguments as spiral_moe_ffn
- * without the workspace. */
+ * capture.  The looked-up address is kept for the process: after
+ * cudaDeviceReset (or any other reset of the device's primary context) do not
+ * call this entry point again in the same process.  All calls share the
+ * array: calls that overlap on the GPU race on it, so order them (one
+ * stream, or events).  As with spiral_moe_ffn, y is valid only while
+ * spiral_device_status reports no error bits: a pipeline wait that gave up
+ * (bit 1) leaves parts of the layer, and so of y, uncomputed.  Arguments as
+ * spiral_moe_ffn without the workspace. */
 SPIRAL_API int spiral_moe_ffn_noalloc(int fmt, const void* w_gate, const void* w_up,
                                       const void* w_down, int64_t n_experts_local,
                                       int64_t expert_first, int64_t hidden, int64_t inter,

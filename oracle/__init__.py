@@ -44,6 +44,8 @@ def lib():
         L.oracle_fp16_to_f32.restype = ctypes.c_float
         L.oracle_f32_to_bf16.argtypes = [ctypes.c_float]
         L.oracle_f32_to_bf16.restype = ctypes.c_uint16
+        L.oracle_threads.argtypes = [i32]
+        L.oracle_threads.restype = i32
         for name in ("oracle_dequant_f32", "oracle_dequant_bf16"):
             f = getattr(L, name)
             f.argtypes = [i32, vp, i64, vp, i64, i64, i32, i32]
@@ -54,6 +56,12 @@ def lib():
             f.restype = None
         _lib = L
     return _lib
+
+
+def threads(n: int = 0) -> int:
+    """Set the OpenMP thread count of the C oracle (n > 0) and return the
+    count in effect."""
+    return int(lib().oracle_threads(int(n)))
 
 
 def _ptr(a: np.ndarray) -> int:

@@ -123,6 +123,18 @@ static void set_threads(int threads) {
 #endif
 }
 
+/* Threads an OpenMP region started now would use (after set_threads), so a
+ * timed CPU baseline can report the cores it really ran on: torchrun sets
+ * OMP_NUM_THREADS=1 in every rank, which the default would silently take. */
+int oracle_threads(int threads) {
+  set_threads(threads);
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
 void oracle_dequant_f32(int fmt, const uint8_t* src, int64_t src_stride, float* out, int64_t K, int64_t N, int ftz,
                         int threads) {
   const int64_t bk = oracle_block_k(fmt), bb = oracle_block_bytes(fmt);

@@ -17,6 +17,8 @@ int64_t oracle_block_k(int fmt);
 int64_t oracle_block_bytes(int fmt);
 float oracle_fp16_to_f32(uint16_t h, int ftz);
 uint16_t oracle_f32_to_bf16(float f);
+/* Sets the OpenMP thread count when threads > 0; returns the count in effect. */
+int oracle_threads(int threads);
 
 /* out[n*K + k] = W[n][k]; src row n at src + n*src_stride. */
 void oracle_dequant_f32(int fmt, const uint8_t* src, int64_t src_stride, float* out, int64_t K, int64_t N, int ftz,

@@ -3,7 +3,10 @@
 Run here, where the reference tree is mounted (it does not exist on the GPU
 box; the fixtures this writes travel instead):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference DIR]
+
+DIR defaults to $SPIRAL_REFERENCE_DIR, else a sibling directory `reference`
+next to this repository.
 
 Everything "expected" below is produced by the reference's NumPy oracle
 (src/quants/tests/formats/{q4_0,q8_0,q6_k}.py) and its mmul harness
@@ -27,6 +30,7 @@ Everything "expected" below is produced by the reference's NumPy oracle
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import json
 import sys
@@ -118,7 +122,8 @@ def edge_raw(fid, rng):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    default_ref = os.environ.get("SPIRAL_REFERENCE_DIR") or str(Path(__file__).resolve().parents[3] / "reference")
+    ap.add_argument("--reference", default=default_ref)
     ap.add_argument("--skip-hashes", action="store_true")
     args = ap.parse_args(argv)
     mods, mmul = load_reference(Path(args.reference))

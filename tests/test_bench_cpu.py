@@ -37,6 +37,38 @@ def test_reference_arm_prints_one_contract_line():
     assert line["gpu_launches"] == 0
 
 
+def test_reference_arm_uses_every_core_under_torchrun():
+    """torchrun exports OMP_NUM_THREADS=1; the CPU arm must still run (and
+    report) one thread per host core, with the GPU arm's config."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    r = _run({"RANK": "0", "WORLD_SIZE": "2", "LOCAL_RANK": "0", "OMP_NUM_THREADS": "1"})
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("{")][0])
+    assert line["cpu_baseline"]["cores"] == (os.cpu_count() or 1)
+    assert line["config"] == bench.headline_config("q4_0", 2)
+
+
+def test_cpu_extras_cover_every_config():
+    """The per-config CPU figures the GPU arm adds at N = 1 (C restatement
+    per config, NumPy dequant and matmul, the reference's own repack)."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    out = bench.cpu_extras(budget_s=0.05)
+    assert set(out["dequant"]) == {"q4_0_4096x4096", "q8_0_14336x4096", "q6_k_14336x4096"}
+    assert set(out["gemm"]) == {"q4_0_M512", "q4_0_M2048", "q6_k_M512", "q6_k_M2048"}
+    assert set(out["moe"]) == {"T1", "T8"}
+    for group in ("dequant", "gemm", "moe"):
+        for v in out[group].values():
+            assert v["value"] > 0 and v["cores"] >= 1
+    assert out["numpy_dequant_q4_0"]["value"] > 0
+    assert out["numpy_matmul_f32_B8"]["value"] > 0
+    for v in out["reference_repack"].values():
+        assert "unavailable" in v or (v["value"] > 0 and v["kind"] == "reference")
+
+
 def test_reference_arm_other_ranks_exit_quietly():
     r = _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert r.returncode == 0, r.stderr[-2000:]

@@ -7,7 +7,9 @@ arena): its scratch is a static 8 MiB array inside the library.  Checked
 through the C-ABI against the workspace entry point (spiral_moe_ffn) with the
 MoE tolerance of tests/test_moe_gpu.py, on two calls in a row with different
 inputs (the shared scratch keeps the first call's contents), and for the
-capacity limit.  Kept in its own file, collected last.
+capacity limit on both sides (107 tokens at config-4 dims fit, 108 do not);
+one call is also checked straight against the float64 oracle.  Kept in its
+own file, collected last.
 """
 
 from __future__ import annotations
@@ -17,6 +19,7 @@ import ctypes
 import numpy as np
 import pytest
 
+import oracle
 import spiral_b200 as sp
 from oracle import formats as F
 
@@ -52,6 +55,43 @@ def test_moe_noalloc_matches_workspace_entry_point_on_two_calls(cuda):
         ok, rel = tolerance_ok(got.cpu().numpy(), want.cpu().numpy().astype(np.float64), bf16_out=False,
                                rel_tol=2e-3)
         assert ok, (call, rel)
+        if call == 1:  # and once straight against the float64 oracle
+            ref = oracle.moe_ffn_f64(fid, F.gen_experts(fid, E, I, H, seed=seed),
+                                     F.gen_experts(fid, E, I, H, seed=seed + 1),
+                                     F.gen_experts(fid, E, H, I, seed=seed + 2),
+                                     F.gen_activations(T, H, seed=seed + 3), ids_np, w_np, H, I, E)
+            ok, rel = tolerance_ok(got.cpu().numpy(), ref, bf16_out=False, rel_tol=2e-3)
+            assert ok, rel
+    assert sp.device_status() == 0
+
+
+def test_moe_noalloc_at_config4_dims_up_to_its_limit(cuda):
+    """Config-4 dims (128 experts, hidden 2048, inter 768, top-8) at 107
+    tokens, the most the static scratch holds, with bf16 output."""
+    import torch
+
+    L = sp.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    fid, E, H, I, topk, T = F.Q4_0, 128, 2048, 768, 8, 107
+    assert sp.moe_workspace_bytes(E, H, I, T, topk) <= 8 << 20
+    # 8 distinct experts repeated 16 times (the content is not what is tested)
+    wg = dev_bytes(np.tile(F.gen_experts(fid, 8, I, H, seed=81), 16))
+    wu = dev_bytes(np.tile(F.gen_experts(fid, 8, I, H, seed=82), 16))
+    wd = dev_bytes(np.tile(F.gen_experts(fid, 8, H, I, seed=83), 16))
+    x = dev_bf16(F.gen_activations(T, H, seed=84)).view(T, H)
+    ids_np, w_np = F.gen_routing(T, E, topk, seed=85)
+    ids, w = torch.from_numpy(ids_np).cuda(), torch.from_numpy(w_np).cuda()
+    want = sp.moe_ffn(fid, wg, wu, wd, x, ids, w, hidden=H, inter=I, n_experts_local=E, y_dtype=sp.BF16)
+    for _ in range(2):
+        got = torch.zeros((T, H), dtype=torch.bfloat16, device="cuda")
+        st = L.spiral_moe_ffn_noalloc(fid, wg.data_ptr(), wu.data_ptr(), wd.data_ptr(), E, 0, H, I, x.data_ptr(),
+                                      x.stride(0), T, ids.data_ptr(), w.data_ptr(), topk, got.data_ptr(), sp.BF16,
+                                      got.stride(0), 0, stream)
+        assert st == 0, L.spiral_last_error()
+        torch.cuda.synchronize()
+        ok, rel = tolerance_ok(got.float().cpu().numpy(), want.float().cpu().numpy().astype(np.float64),
+                               bf16_out=True, rel_tol=2e-3)
+        assert ok, rel
     assert sp.device_status() == 0
 
 
