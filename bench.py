@@ -809,13 +809,13 @@ def bench_moe(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_kind, 
     2,654,208 B per layer / time.  8 copies of the expert weights and 8
     routings rotate, so a layer's experts were last touched >= 8 layers ago
     (>= 168 MB of other weights: not in L2).  At N > 1 the experts are
-    sharded (rank r owns 128/N of them), every rank holds the T tokens, runs
-    its experts into an fp32 partial and the partials are summed over NCCL
-    (all_reduce); U per rank is reported."""
+    sharded (rank r owns 128/N of them), every rank holds the T tokens and
+    spiral_moe_ffn_ep runs its experts and combines the ranks' partials in
+    one kernel over NVLink (reduce-scatter + all-gather of fp32 units); U per
+    rank is reported."""
     import torch
-    import torch.distributed as dist
 
-    from spiral_b200.dist import expert_range
+    from spiral_b200.dist import MoeExchange, expert_range
 
     fid, E, H, I, topk, routings = F.Q4_0, MOE_E, MOE_H, MOE_I, MOE_TOPK, 8
     e0, e1 = expert_range(E, world, rank)
@@ -831,6 +831,7 @@ def bench_moe(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_kind, 
     wg = [g0] + [g0.clone() for _ in range(copies - 1)]
     wu = [u0] + [u0.clone() for _ in range(copies - 1)]
     wd = [d0] + [d0.clone() for _ in range(copies - 1)]
+    mx = MoeExchange(H, max(Ts), dev) if world > 1 else None
     res = {}
     for T in Ts:
         x = torch.from_numpy(F.gen_activations(T, H, seed=T).view(np.int16)).to(dev).view(torch.bfloat16)
@@ -839,15 +840,18 @@ def bench_moe(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_kind, 
         uloc = [len({int(v) for v in ids.reshape(-1) if e0 <= v < e1}) for ids, _ in rts]
         ids = [torch.from_numpy(a).to(dev) for a, _ in rts]
         wts = [torch.from_numpy(b).to(dev) for _, b in rts]
-        y = torch.empty((T, H), dtype=torch.bfloat16 if world == 1 else torch.float32, device=dev)
+        y = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
         ws = torch.empty(sp.moe_workspace_bytes(El, H, I, T, topk), dtype=torch.uint8, device=dev)
 
         def body(i, x=x, ids=ids, wts=wts, y=y, ws=ws):
             c, r = i % copies, (i // copies) % routings
-            sp.moe_ffn(fid, wg[c], wu[c], wd[c], x, ids[r], wts[r], hidden=H, inter=I, n_experts_local=El,
-                       expert_first=e0, y=y, y_dtype=sp.BF16 if world == 1 else sp.F32, workspace=ws)
-            if world > 1:
-                dist.all_reduce(y)
+            if world == 1:
+                sp.moe_ffn(fid, wg[c], wu[c], wd[c], x, ids[r], wts[r], hidden=H, inter=I, n_experts_local=El,
+                           expert_first=e0, y=y, workspace=ws)
+            else:
+                sp.moe_ffn_ep(fid, wg[c], wu[c], wd[c], x, ids[r], wts[r], hidden=H, inter=I, n_experts_local=El,
+                              expert_first=e0, exchange_peers_dev=mx.peers, rank=rank, world=world,
+                              max_tokens=mx.max_tokens, y=y, workspace=ws)
 
         steps = copies * routings  # one graph: every (copy, routing) pair once
         t = timer.timed(steps, 3, body, gsteps=steps) / steps * 1e-3
@@ -860,9 +864,12 @@ def bench_moe(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_kind, 
         res[f"T{T}"] = {"us": t * 1e6, "unique_experts": u_mean, "unique_experts_per_rank": ul_mean,
                         "weight_GBps": wbytes / t / 1e9,
                         "roofline": roofline("hbm", alg, t, hbm_peak, peak_kind, "moe layer (4 kernels)"
-                                             if world == 1 else "moe layer + NCCL all_reduce",
+                                             if world == 1 else "moe layer, combine fused over NVLink",
                                              profile_traffic(f"moe_T{T}_E{El}"))}
     del wg, wu, wd
+    if mx is not None:
+        torch.cuda.synchronize()
+        del mx
     return res
 
 

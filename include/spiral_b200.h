@@ -134,9 +134,18 @@ SPIRAL_API int64_t spiral_quants_packed_bytes(int fmt, int64_t weights_rows,
 
 /* Device-side repack of a (possibly padded) canonical tensor view into the
  * dense device layout every kernel here reads: weights_cols rows of
- * packed_bytes/weights_cols bytes.  `src` and `dst` are device pointers;
- * src_col_stride_bytes >= the dense row size.  Returns bytes written, or 0 on
- * invalid dims, insufficient capacity, null pointers or a CUDA error.
+ * packed_bytes/weights_cols bytes.  `src` and `dst` are device pointers
+ * (2-byte aligned); src_col_stride_bytes >= the dense row size and even.
+ * As the reference's repack does, subnormal fp16 scales are flushed to +0
+ * (its device path decodes exponent 0 as zero; q4_0/repack.h:75-80,
+ * q6_k/repack.h:64-67) and Q8_0 quants of -128 are kept but reported
+ * (q8_0/repack.h:76-78): at most one warning line per call, worded as the
+ * reference's (common/repack.h:36-58), goes to the hook set by
+ * spiral_set_repack_warn (default: stderr).  The call synchronizes `stream`
+ * (it must read the device's report before it returns, as the reference's
+ * host repack returns only when done).  Returns bytes written, or 0 on
+ * invalid dims, insufficient capacity, null or misaligned pointers or a CUDA
+ * error.
  * Replaces: extern "C" int64_t quants_repack(src, src_col_stride_bytes, dst,
  *           dst_capacity, rows, cols) (src/quants/tests/repack.cc:23-32,
  *           q4_0/repack.h:27-41).  Same argument meaning and return contract;
@@ -145,6 +154,14 @@ SPIRAL_API int64_t spiral_quants_repack(int fmt, const void* src,
                              int64_t src_col_stride_bytes, void* dst,
                              int64_t dst_capacity, int64_t weights_rows,
                              int64_t weights_cols, void* stream);
+
+/* Receiver of the repack's one-line warnings ('\n'-terminated text).
+ * Replaces the reference's overridable QUANTS_REPACK_WARN macro
+ * (src/quants/common/repack.h:9-14): pass a function to route the line into
+ * the caller's logger, or NULL to suppress it; the default writes to stderr.
+ * Process-wide; the hook may be called from any host thread that repacks. */
+typedef void (*spiral_repack_warn_fn_t)(const char* line, void* user);
+SPIRAL_API void spiral_set_repack_warn(spiral_repack_warn_fn_t fn, void* user);
 
 /* ------------------------------------------------------ dequant-to-bf16 -- */
 
@@ -225,6 +242,34 @@ SPIRAL_API int spiral_mul_mat_allgather(int fmt, const void* w_shard, int64_t w_
                                         void* const* exchange_peers, int rank, int world,
                                         unsigned flags, void* stream);
 
+/* ggml backend boundary.  A tensor as a ggml backend sees it: ggml type id,
+ * elements per dimension (ne[0] innermost) and bytes between consecutive
+ * elements of each dimension (nb[0] = block bytes for a quantized row,
+ * element size otherwise), data on the device.  Field meaning as ggml's
+ * struct ggml_tensor, so a backend fills it from its node's tensors. */
+typedef struct spiral_ggml_tensor {
+  int32_t type;
+  int64_t ne[4];
+  size_t nb[4];
+  void* data;
+} spiral_ggml_tensor;
+
+/* supports_op for GGML_OP_MUL_MAT: 1 when spiral_ggml_mul_mat serves the
+ * node (src0 Q4_0 / Q8_0 / Q6_K, src1 BF16, dst F32 or BF16, rows
+ * contiguous along K, ggml's shape and broadcast rules), else 0.  The
+ * reference's planned llama.cpp backend (README.md:11-14, TODO.md:49-55)
+ * offers these src0 types to ggml the same way. */
+SPIRAL_API int spiral_ggml_supports_mul_mat(const spiral_ggml_tensor* src0, const spiral_ggml_tensor* src1,
+                                            const spiral_ggml_tensor* dst);
+
+/* GGML_OP_MUL_MAT with ggml's semantics: for every batch (i2, i3) of src1,
+ *   dst[i3][i2][i1][i0] = sum_k src0[i3/r3][i2/r2][i0][k] * src1[i3][i2][i1][k]
+ * (r2 = ne12/ne02, r3 = ne13/ne03: src0 broadcast over the batch dims), each
+ * batch one spiral_mul_mat (same numerics and flags).  Returns the first
+ * non-zero status, or the status that supports_mul_mat refuses with. */
+SPIRAL_API int spiral_ggml_mul_mat(const spiral_ggml_tensor* src0, const spiral_ggml_tensor* src1,
+                                   spiral_ggml_tensor* dst, unsigned flags, void* stream);
+
 /* Fused unpack + mmul in the reference's tiled I/O orders:
  *   inputs  bf16 [weights_rows/8][inputs_vecs][8]
  *   outputs f32  [weights_cols/8][inputs_vecs][8], ACCUMULATED (+=); the
@@ -272,6 +317,47 @@ SPIRAL_API int spiral_moe_ffn(int fmt, const void* w_gate, const void* w_up, con
                               const float* expert_weights, int64_t topk, void* y, int y_dtype,
                               int64_t y_row_stride_elems, void* workspace,
                               int64_t workspace_bytes, unsigned flags, void* stream);
+
+/* Bytes of one rank's exchange buffer for spiral_moe_ffn_ep (0 if invalid:
+ * non-positive dims).  Sized for up to max_tokens tokens per call. */
+SPIRAL_API int64_t spiral_moe_ep_exchange_bytes(int64_t hidden, int64_t max_tokens);
+
+/* Expert-parallel MoE FFN layer, one process per GPU (BASELINE config 4 at
+ * 2..8 GPUs; the reference has no MoE and no multi-device path, its
+ * multi-tile pattern splits weights and broadcasts the input,
+ * src/quants/tests/poc/calc.py:1-11, 154-215).  Every rank passes the same
+ * tokens: x [tokens][hidden], expert_ids and expert_weights [tokens][topk]
+ * (global expert ids), as they are after the preceding dense layer's
+ * all-gather; rank r holds the experts [expert_first, expert_first +
+ * n_experts_local) in w_gate / w_up / w_down as spiral_moe_ffn takes them.
+ * Each rank runs its local experts (spiral_moe_ffn's kernels, ids of other
+ * ranks' experts skipped), then one kernel combines the ranks' fp32 partial
+ * layers over NVLink: the partials of each column go to the column's owner
+ * (hidden / world columns each), which sums them in rank order and sends
+ * the sum to every rank.  On return every rank's y holds the whole layer
+ * output, identical on all ranks: for every token, the sum over all its topk
+ * slots (slots of one rank in slot order, ranks in rank order), stored as
+ * y_dtype (ACCUMULATE adds into an F32 y).  With top-8 of 128 experts over
+ * at most 8 ranks nearly every token reaches every rank, so the tokens are
+ * replicated rather than dispatched with an all-to-all.
+ * exchange_peers: DEVICE array of `world` device pointers, rank r's exchange
+ * buffer (spiral_moe_ep_exchange_bytes(hidden, max_tokens) bytes, 16-byte
+ * aligned, peer-mapped on every rank, zeroed once before the first call);
+ * tokens <= max_tokens; hidden a multiple of world.  Every rank makes the
+ * same calls in the same order with no other kernel running on its GPU
+ * meanwhile, and calls on one exchange never overlap.  A rank that does not
+ * arrive makes the others' bounded waits (2 s) give up with bit 8 of
+ * spiral_device_status; y is then invalid, later calls skip their waits until
+ * the status is read, and the exchanges must be zeroed again on every rank.
+ * Other arguments and the workspace as spiral_moe_ffn. */
+SPIRAL_API int spiral_moe_ffn_ep(int fmt, const void* w_gate, const void* w_up, const void* w_down,
+                                 int64_t n_experts_local, int64_t expert_first, int64_t hidden,
+                                 int64_t inter, const void* x, int64_t x_row_stride_elems,
+                                 int64_t tokens, int64_t max_tokens, const int32_t* expert_ids,
+                                 const float* expert_weights, int64_t topk, void* y, int y_dtype,
+                                 int64_t y_row_stride_elems, void* const* exchange_peers, int rank,
+                                 int world, void* workspace, int64_t workspace_bytes, unsigned flags,
+                                 void* stream);
 
 /* The same MoE layer for callers that cannot allocate device memory when they
  * call in: a plain C host handed device pointers with no allocator of its own,

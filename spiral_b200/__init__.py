@@ -40,9 +40,12 @@ _SIGNATURES = {
     "spiral_quants_record_count": ([_i32, _i64, _i64], _i64),
     "spiral_quants_packed_bytes": ([_i32, _i64, _i64], _i64),
     "spiral_quants_repack": ([_i32, _vp, _i64, _vp, _i64, _i64, _i64, _vp], _i64),
+    "spiral_set_repack_warn": ([_vp, _vp], None),
     "spiral_dequant_bf16": ([_i32, _vp, _i64, _vp, _i64, _i64, _i64, _u32, _vp], _i32),
     "spiral_quants_unpack_all": ([_i32, _vp, _vp, _i64, _i64, _u32, _vp], _i32),
     "spiral_mul_mat": ([_i32, _vp, _i64, _vp, _i64, _vp, _i32, _i64, _i64, _i64, _i64, _u32, _vp], _i32),
+    "spiral_ggml_supports_mul_mat": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], _i32),
+    "spiral_ggml_mul_mat": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _u32, _vp], _i32),
     "spiral_quants_unpack_mmul_all": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _u32, _vp], _i32),
     "spiral_allgather_exchange_bytes": ([_i64], _i64),
     "spiral_mul_mat_allgather": ([_i32, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i32,
@@ -50,9 +53,21 @@ _SIGNATURES = {
     "spiral_moe_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64], _i64),
     "spiral_moe_ffn": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i32,
                         _i64, _vp, _i64, _u32, _vp], _i32),
+    "spiral_moe_ep_exchange_bytes": ([_i64, _i64], _i64),
+    "spiral_moe_ffn_ep": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp,
+                           _i32, _i64, _vp, _i32, _i32, _vp, _i64, _u32, _vp], _i32),
     "spiral_moe_ffn_noalloc": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp,
                                 _i32, _i64, _u32, _vp], _i32),
 }
+
+
+
+class GgmlTensor(ctypes.Structure):
+    """spiral_ggml_tensor: ggml type id, ne[4], nb[4] (bytes), device data."""
+
+    _fields_ = [("type", ctypes.c_int32), ("ne", ctypes.c_int64 * 4), ("nb", ctypes.c_size_t * 4),
+                ("data", ctypes.c_void_p)]
+
 
 _lib = None
 
@@ -135,6 +150,25 @@ def repack(fmt, src, src_col_stride_bytes: int, dst, dst_capacity: int, weights_
     """Bytes written, 0 on invalid input (reference repack contract)."""
     return lib().spiral_quants_repack(fmt_id(fmt), _ptr(src), src_col_stride_bytes, _ptr(dst), dst_capacity,
                                       weights_rows, weights_cols, _stream(stream))
+
+
+# C signature of the repack warning hook: void (*)(const char* line, void* user)
+REPACK_WARN_FN = ctypes.CFUNCTYPE(None, ctypes.c_char_p, ctypes.c_void_p)
+_warn_keep = None  # the installed ctypes callback must outlive its use
+
+
+def set_repack_warn(fn=None, *, to_stderr: bool = False) -> None:
+    """Route the repack's one-line warnings: fn(line: str) receives each
+    line; fn=None suppresses them; to_stderr=True writes them to sys.stderr
+    (the library's own default, before any call here, is the C stderr)."""
+    global _warn_keep
+    if to_stderr:
+        import sys
+
+        fn = sys.stderr.write
+    cb = None if fn is None else REPACK_WARN_FN(lambda line, user: fn(line.decode()))
+    _warn_keep = cb
+    lib().spiral_set_repack_warn(ctypes.cast(cb, ctypes.c_void_p) if cb is not None else None, None)
 
 
 def device_status(stream=None) -> int:
@@ -258,3 +292,61 @@ def moe_ffn(fmt, w_gate, w_up, w_down, x, expert_ids, expert_weights, *, hidden:
                                 _ptr(y), y_dtype, int(y.stride(0)), _ptr(workspace), int(workspace.numel()),
                                 flags, _stream(stream)))
     return y
+
+
+def moe_ep_exchange_bytes(hidden: int, max_tokens: int) -> int:
+    return int(lib().spiral_moe_ep_exchange_bytes(hidden, max_tokens))
+
+
+def moe_ffn_ep(fmt, w_gate, w_up, w_down, x, expert_ids, expert_weights, *, hidden: int, inter: int,
+               n_experts_local: int, expert_first: int, exchange_peers_dev, rank: int, world: int, max_tokens: int,
+               y=None, y_dtype: int = BF16, workspace=None, accumulate: bool = False, ftz: bool = False,
+               stream=None):
+    """Expert-parallel MoE layer (one process per GPU): every rank passes the
+    same x [T][hidden] / ids / weights and its expert range; y receives the
+    whole layer (all ranks' experts), identical on every rank.  See
+    spiral_b200.dist.MoeExchange for the exchange buffers."""
+    import torch
+
+    f = fmt_id(fmt)
+    T, topk = int(expert_ids.shape[0]), int(expert_ids.shape[1])
+    if y is None:
+        y = torch.empty((T, hidden), dtype=torch.bfloat16 if y_dtype == BF16 else torch.float32, device=x.device)
+    need = moe_workspace_bytes(n_experts_local, hidden, inter, T, topk)
+    if workspace is None:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+    flags = (FLAG_FTZ_SCALES if ftz else 0) | (FLAG_ACCUMULATE if accumulate else 0)
+    _check(lib().spiral_moe_ffn_ep(f, _ptr(w_gate), _ptr(w_up), _ptr(w_down), n_experts_local, expert_first, hidden,
+                                   inter, _ptr(x), int(x.stride(0)), T, max_tokens, _ptr(expert_ids),
+                                   _ptr(expert_weights), topk, _ptr(y), y_dtype, int(y.stride(0)),
+                                   _ptr(exchange_peers_dev), rank, world, _ptr(workspace), int(workspace.numel()),
+                                   flags, _stream(stream)))
+    return y
+
+
+# ------------------------------------------------------------ ggml boundary
+
+
+def ggml_tensor(type_id: int, ne, nb, data) -> GgmlTensor:
+    """A spiral_ggml_tensor from ggml-style ne/nb (innermost first) and a
+    device pointer (int or tensor)."""
+    t = GgmlTensor()
+    t.type = int(type_id)
+    ne = list(ne) + [1] * (4 - len(ne))
+    nb = list(nb) + [0] * (4 - len(nb))
+    for i in range(4):
+        t.ne[i] = int(ne[i])
+        t.nb[i] = int(nb[i])
+    t.data = _ptr(data)
+    return t
+
+
+def ggml_supports_mul_mat(src0: GgmlTensor, src1: GgmlTensor, dst: GgmlTensor) -> bool:
+    return bool(lib().spiral_ggml_supports_mul_mat(ctypes.byref(src0), ctypes.byref(src1), ctypes.byref(dst)))
+
+
+def ggml_mul_mat(src0: GgmlTensor, src1: GgmlTensor, dst: GgmlTensor, *, ftz: bool = False,
+                 accumulate: bool = False, stream=None) -> None:
+    flags = (FLAG_FTZ_SCALES if ftz else 0) | (FLAG_ACCUMULATE if accumulate else 0)
+    _check(lib().spiral_ggml_mul_mat(ctypes.byref(src0), ctypes.byref(src1), ctypes.byref(dst), flags,
+                                     _stream(stream)))

@@ -145,16 +145,19 @@ int64_t spiral_quants_repack(int fmt, const void* src, int64_t src_col_stride_by
   if (bytes == 0 || src == nullptr || dst == nullptr || bytes > dst_capacity) return 0;
   const int64_t rb = row_bytes(fmt, weights_rows);
   if (src_col_stride_bytes < rb) return 0;
-  const cudaError_t e =
-      cudaMemcpy2DAsync(dst, static_cast<size_t>(rb), src, static_cast<size_t>(src_col_stride_bytes),
-                        static_cast<size_t>(rb), static_cast<size_t>(weights_cols), cudaMemcpyDefault,
-                        static_cast<cudaStream_t>(stream));
+  if ((reinterpret_cast<uintptr_t>(src) & 1u) || (reinterpret_cast<uintptr_t>(dst) & 1u) ||
+      (src_col_stride_bytes & 1))
+    return 0;
+  const cudaError_t e = repack(fmt, src, src_col_stride_bytes, dst, weights_rows, weights_cols,
+                               static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
-    cuda_fail(e, "repack copy");
+    cuda_fail(e, "repack");
     return 0;
   }
   return bytes;
 }
+
+void spiral_set_repack_warn(spiral_repack_warn_fn_t fn, void* user) { repack_set_warn(fn, user); }
 
 int spiral_dequant_bf16(int fmt, const void* src, int64_t src_row_stride_bytes, void* dst,
                         int64_t dst_row_stride_elems, int64_t K, int64_t N, unsigned flags, void* stream) {
@@ -390,6 +393,61 @@ int spiral_moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w_
               (flags & SPIRAL_FLAG_FTZ_SCALES) != 0, tokens, topk, hidden, inter, expert_first, n_experts_local,
               workspace, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "moe launch");
+  return SPIRAL_OK;
+}
+
+int64_t spiral_moe_ep_exchange_bytes(int64_t hidden, int64_t max_tokens) {
+  if (hidden <= 0 || max_tokens <= 0 || max_tokens > (int64_t(1) << 24) || hidden > (int64_t(1) << 20)) return 0;
+  return moe_ep_xchg_bytes(hidden, max_tokens);
+}
+
+int spiral_moe_ffn_ep(int fmt, const void* w_gate, const void* w_up, const void* w_down, int64_t n_experts_local,
+                      int64_t expert_first, int64_t hidden, int64_t inter, const void* x, int64_t x_row_stride_elems,
+                      int64_t tokens, int64_t max_tokens, const int32_t* expert_ids, const float* expert_weights,
+                      int64_t topk, void* y, int y_dtype, int64_t y_row_stride_elems, void* const* exchange_peers,
+                      int rank, int world, void* workspace, int64_t workspace_bytes, unsigned flags, void* stream) {
+  g_last_error[0] = 0;
+  if (world < 1 || world > 64 || rank < 0 || rank >= world)
+    return fail(SPIRAL_ERR_INVALID_ARGUMENT, "rank %d / world %d", rank, world);
+  if (exchange_peers == nullptr) return fail(SPIRAL_ERR_NULL_POINTER, "null exchange_peers");
+  if (tokens > max_tokens) return fail(SPIRAL_ERR_CAPACITY, "tokens %lld > max_tokens %lld", (long long)tokens,
+                                        (long long)max_tokens);
+  if (hidden % world != 0)
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "hidden %lld is not a multiple of world %d", (long long)hidden, world);
+  // the remaining rules are spiral_moe_ffn's
+  if (!fmt_valid(fmt)) return fail(SPIRAL_ERR_INVALID_FORMAT, "unknown quantized format %d", fmt);
+  if (n_experts_local <= 0 || expert_first < 0 || tokens <= 0 || topk <= 0 || topk > 64 || hidden <= 0 ||
+      inter <= 0 || n_experts_local > 4096 || tokens > (int64_t(1) << 24))
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "bad MoE dims (experts %lld, tokens %lld, topk %lld)",
+                (long long)n_experts_local, (long long)tokens, (long long)topk);
+  if (!moe_shape_ok(fmt, hidden, inter))
+    return fail(SPIRAL_ERR_INVALID_SHAPE,
+                "hidden=%lld / inter=%lld: need multiples of %d, hidden <= 4096 and inter <= 2048",
+                (long long)hidden, (long long)inter, fmt == SPIRAL_QFMT_Q6_K ? 2048 : 256);
+  if (!w_gate || !w_up || !w_down || !x || !expert_ids || !expert_weights || !y || !workspace)
+    return fail(SPIRAL_ERR_NULL_POINTER, "null MoE operand");
+  if (y_dtype != SPIRAL_DTYPE_BF16 && y_dtype != SPIRAL_DTYPE_F32)
+    return fail(SPIRAL_ERR_INVALID_ARGUMENT, "y_dtype %d is neither F32 nor BF16", y_dtype);
+  if ((flags & SPIRAL_FLAG_ACCUMULATE) && y_dtype != SPIRAL_DTYPE_F32)
+    return fail(SPIRAL_ERR_INVALID_ARGUMENT, "ACCUMULATE needs an F32 destination");
+  if (x_row_stride_elems < hidden || y_row_stride_elems < hidden)
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "x/y row strides smaller than hidden");
+  const auto al = [](const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
+  if (!al(w_gate, 16) || !al(w_up, 16) || !al(w_down, 16) || !al(x, 16) || (x_row_stride_elems % 8) != 0 ||
+      !al(expert_ids, 4) || !al(expert_weights, 4) || !al(workspace, 256) ||
+      !al(y, y_dtype == SPIRAL_DTYPE_F32 ? 4 : 2))
+    return fail(SPIRAL_ERR_ALIGNMENT, "MoE operands misaligned (weights, x rows 16 B; workspace 256 B)");
+  const int64_t need = spiral_moe_workspace_bytes(n_experts_local, hidden, inter, tokens, topk);
+  if (workspace_bytes < need)
+    return fail(SPIRAL_ERR_CAPACITY, "workspace %lld bytes < %lld needed", (long long)workspace_bytes,
+                (long long)need);
+  const cudaError_t e = moe_ffn_ep(fmt, w_gate, w_up, w_down, x, x_row_stride_elems, expert_ids, expert_weights, y,
+                                   y_row_stride_elems, y_dtype == SPIRAL_DTYPE_BF16,
+                                   (flags & SPIRAL_FLAG_ACCUMULATE) != 0, (flags & SPIRAL_FLAG_FTZ_SCALES) != 0,
+                                   tokens, topk, hidden, inter, expert_first, n_experts_local, workspace,
+                                   reinterpret_cast<uint8_t* const*>(exchange_peers), rank, world, max_tokens,
+                                   static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "moe ep launch");
   return SPIRAL_OK;
 }
 

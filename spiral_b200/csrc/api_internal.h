@@ -8,6 +8,8 @@
 #include <algorithm>
 #include <cstdint>
 
+#include "../../include/spiral_b200.h"
+
 namespace spiral {
 
 // dequant.cu
@@ -53,9 +55,33 @@ struct PeerOut {
 int64_t gemv_xchg_bytes(int64_t n_total);
 cudaError_t gemv_allgather(const MatArgs& a, const PeerOut& po, cudaStream_t stream);
 
+// Exchange buffer of the gathered GEMV (one per rank, peer-mapped): a
+// 256-byte control block (word 0: calls completed on this rank, word 1: CTA
+// count of the running call) and two slots (call parity) of [8][n_total / 2]
+// units.  A unit is 8 bytes, two bf16 outputs (columns 2u, 2u + 1) in the
+// low word and the call's flag (call count | 2^31) in the high word, stored
+// and loaded as one 64-bit access, so a reader that sees the flag sees the
+// data: no fence is needed on either side.  Units travel in 16-byte pairs.
+constexpr int64_t kGemvXchgCtrlBytes = 256;
+__host__ __device__ constexpr int64_t gemv_xchg_slot_bytes(int64_t n_total) { return 8 * n_total * 4; }
+
+// gemv_xs.cu — activation-stationary GEMV for Q4_0 / Q8_0 at K in {1024,
+// 2048, 4096}; gemv() and gemv_allgather() use it whenever it applies.
+// po == nullptr: plain MUL_MAT; else the row-sharded call with the
+// all-gather fused in (same exchange protocol as above).
+bool gemv_xs_ok(const MatArgs& a);
+cudaError_t gemv_xs(const MatArgs& a, const PeerOut* po, cudaStream_t stream);
+
 // gemm.cu — tcgen05 dequant-GEMM for larger M.
 bool gemm_supported(const MatArgs& a);
 cudaError_t gemm(const MatArgs& a, cudaStream_t stream);
+
+// repack.cu — canonical view -> dense canonical tensor with the reference's
+// subnormal-scale flush and -128 report; synchronizes `stream` and emits at
+// most one warning line through the hook.
+cudaError_t repack(int fmt, const void* src, int64_t src_stride, void* dst, int64_t K, int64_t N,
+                   cudaStream_t stream);
+void repack_set_warn(spiral_repack_warn_fn_t fn, void* user);
 
 // moe.cu — MoE FFN decode layer over quantized experts.
 size_t moe_workspace_bytes(int64_t E_local, int64_t H, int64_t I, int64_t T, int64_t topk);
@@ -64,6 +90,16 @@ cudaError_t moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w
                     int64_t x_stride, const int32_t* ids, const float* wts, void* y, int64_t y_stride, bool y_bf16,
                     bool accumulate, bool ftz, int64_t T, int64_t topk, int64_t H, int64_t I, int64_t e0,
                     int64_t E_local, void* ws, cudaStream_t stream);
+
+// Expert-parallel MoE layer: the local experts' layer plus a fused combine
+// of every rank's fp32 partial over peer-mapped exchange buffers
+// (moe_ep_xchg_bytes each, zeroed before first use); y gets the whole layer.
+int64_t moe_ep_xchg_bytes(int64_t H, int64_t max_tokens);
+cudaError_t moe_ffn_ep(int fmt, const void* w_gate, const void* w_up, const void* w_down, const void* x,
+                       int64_t x_stride, const int32_t* ids, const float* wts, void* y, int64_t y_stride, bool y_bf16,
+                       bool accumulate, bool ftz, int64_t T, int64_t topk, int64_t H, int64_t I, int64_t e0,
+                       int64_t E_local, void* ws, uint8_t* const* peers, int rank, int world, int64_t max_tokens,
+                       cudaStream_t stream);
 
 // Allocation-free MoE: capacity and device address (current device) of the
 // library's static scratch array.

@@ -80,15 +80,10 @@ struct GemvParams {
   int rank, world;
 };
 
-// Exchange buffer of the gathered GEMV (one per rank, peer-mapped): a
-// 256-byte control block (word 0: calls completed on this rank, word 1: CTA
-// count of the running call) and two slots (call parity) of [8][n_total / 2]
-// units.  A unit is 8 bytes, two bf16 outputs (columns 2u, 2u + 1) in the
-// low word and the call's flag in the high word, stored and loaded as one
-// 64-bit access, so a reader that sees the flag sees the data: no fence is
-// needed on either side.  Units travel in 16-byte pairs (4 columns).
-constexpr int64_t kXchgCtrlBytes = 256;
-__host__ __device__ constexpr int64_t xchg_slot_bytes(int64_t n_total) { return 8 * n_total * 4; }
+// Exchange buffer layout: kGemvXchgCtrlBytes / gemv_xchg_slot_bytes
+// (api_internal.h).
+constexpr int64_t kXchgCtrlBytes = kGemvXchgCtrlBytes;
+__host__ __device__ constexpr int64_t xchg_slot_bytes(int64_t n_total) { return gemv_xchg_slot_bytes(n_total); }
 
 __device__ __forceinline__ uint32_t xchg_flag(uint32_t calls) { return calls | 0x80000000u; }
 
@@ -508,6 +503,7 @@ bool gemv_fast_ok(const MatArgs& a) {
 template <int FMT>
 static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream, const PeerOut* po = nullptr) {
   using F = GemvFmt<FMT>;
+  if (gemv_xs_ok(a)) return gemv_xs(a, po, stream);
   GemvPlan plan;
   if (reinterpret_cast<uintptr_t>(a.w) % 16 != 0 || a.w_stride % 16 != 0 || !gemv_plan<FMT>(a, &plan)) {
     if (po != nullptr) return cudaErrorNotSupported;

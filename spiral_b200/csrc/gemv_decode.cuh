@@ -91,6 +91,12 @@ template <>
 struct GroupDecoder<kQ4_0> {
   __device__ __forceinline__ static void run(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg, bool ftz,
                                              float (&acc)[4]) {
+    run_b(ra, rb, c, [xg](int s) { return *reinterpret_cast<const uint2*>(xg + 32 * s); }, ftz, acc);
+  }
+  // bx(s): this lane's B fragment of step s (the activations of xk(s, c)).
+  template <class BX>
+  __device__ __forceinline__ static void run_b(const uint8_t* ra, const uint8_t* rb, int c, BX&& bx, bool ftz,
+                                               float (&acc)[4]) {
     // qs starts at 18c + 2: 4-byte aligned for odd c, 2 mod 4 for even c.
     const int woff = 18 * c + 2 * (c & 1);
     const uint32_t sh = (c & 1) ? 0u : 16u;
@@ -120,12 +126,12 @@ struct GroupDecoder<kQ4_0> {
     for (int j = 0; j < 4; ++j) {
       const uint32_t la = qa[j] & 0x0F0F0F0Fu, ha = qa[j] & 0xF0F0F0F0u;
       const uint32_t lb = qb[j] & 0x0F0F0F0Fu, hb = qb[j] & 0xF0F0F0F0u;
-      const uint2 b0 = *reinterpret_cast<const uint2*>(xg + 32 * (2 * j));
+      const uint2 b0 = bx(2 * j);
       mma_bf16_16816(acc, fma2_pack(byte_to_f1<0>(la), byte_to_f1<1>(la), DLa, CLa),
                      fma2_pack(byte_to_f1<0>(lb), byte_to_f1<1>(lb), DLb, CLb),
                      fma2_pack(byte_to_f1<2>(la), byte_to_f1<3>(la), DLa, CLa),
                      fma2_pack(byte_to_f1<2>(lb), byte_to_f1<3>(lb), DLb, CLb), b0.x, b0.y);
-      const uint2 b1 = *reinterpret_cast<const uint2*>(xg + 32 * (2 * j + 1));
+      const uint2 b1 = bx(2 * j + 1);
       mma_bf16_16816(acc, fma2_pack(byte_to_f1<0>(ha), byte_to_f1<1>(ha), DHa, CHa),
                      fma2_pack(byte_to_f1<0>(hb), byte_to_f1<1>(hb), DHb, CHb),
                      fma2_pack(byte_to_f1<2>(ha), byte_to_f1<3>(ha), DHa, CHa),
@@ -142,6 +148,11 @@ template <>
 struct GroupDecoder<kQ8_0> {
   __device__ __forceinline__ static void run(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg, bool ftz,
                                              float (&acc)[4]) {
+    run_b(ra, rb, c, [xg](int s) { return *reinterpret_cast<const uint2*>(xg + 32 * s); }, ftz, acc);
+  }
+  template <class BX>
+  __device__ __forceinline__ static void run_b(const uint8_t* ra, const uint8_t* rb, int c, BX&& bx, bool ftz,
+                                               float (&acc)[4]) {
     const int woff = 34 * c + 2 * (c & 1);
     const uint32_t sh = (c & 1) ? 0u : 16u;
     const float da = fp16_bits_to_f32(lds_u16(ra + 34 * c), ftz);
@@ -156,7 +167,7 @@ struct GroupDecoder<kQ8_0> {
       const uint32_t qb = __funnelshift_r(pb, nb, sh) ^ 0x80808080u;
       pa = na;
       pb = nb;
-      const uint2 b = *reinterpret_cast<const uint2*>(xg + 32 * s);
+      const uint2 b = bx(s);
       mma_bf16_16816(acc, fma2_pack(byte_to_f1<0>(qa), byte_to_f1<1>(qa), Da, Ca),
                      fma2_pack(byte_to_f1<0>(qb), byte_to_f1<1>(qb), Db, Cb),
                      fma2_pack(byte_to_f1<2>(qa), byte_to_f1<3>(qa), Da, Ca),
@@ -186,6 +197,11 @@ struct GroupDecoder<kQ6_K> {
   }
   __device__ __forceinline__ static void run(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg, bool ftz,
                                              float (&acc)[4], uint32_t sh) {
+    run_b(ra, rb, c, [xg](int t) { return *reinterpret_cast<const uint2*>(xg + 32 * t); }, ftz, acc, sh);
+  }
+  template <class BX>
+  __device__ __forceinline__ static void run_b(const uint8_t* ra, const uint8_t* rb, int c, BX&& bx, bool ftz,
+                                               float (&acc)[4], uint32_t sh) {
     const float da = fp16_bits_to_f32(lds_u16(ra + 208), ftz);
     const float db = fp16_bits_to_f32(lds_u16(rb + 208), ftz);
 #pragma unroll
@@ -214,7 +230,7 @@ struct GroupDecoder<kQ6_K> {
         for (int s = 0; s < 4; ++s) {
           const uint32_t qa = assemble((s & 1) ? qlb[half] : qla[half], qha[half], s);
           const uint32_t qb = assemble((s & 1) ? qlb_b[half] : qla_b[half], qh_b[half], s);
-          const uint2 b = *reinterpret_cast<const uint2*>(xg + 32 * (8 * h + 4 * half + s));
+          const uint2 b = bx(8 * h + 4 * half + s);
           mma_bf16_16816(acc, fma2_pack(byte_to_f2<0>(qa), byte_to_f2<1>(qa), Da[s], Ca[s]),
                          fma2_pack(byte_to_f2<0>(qb), byte_to_f2<1>(qb), Db[s], Cb[s]),
                          fma2_pack(byte_to_f2<2>(qa), byte_to_f2<3>(qa), Da[s], Ca[s]),

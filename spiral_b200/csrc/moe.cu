@@ -420,6 +420,141 @@ __global__ void moe_combine(const MoeArgs a) {
   }
 }
 
+// ------------------------------------------------- expert-parallel combine --
+//
+// Expert-parallel layer (spiral_moe_ffn_ep): every rank holds all T tokens
+// (x, ids and weights replicated, as after the preceding dense layer's
+// all-gather) and the experts [e0, e0 + E_local); its partial y_r[t][h] is
+// the sum over the token's slots whose expert is local.  The ranks' partials
+// are combined inside this kernel over NVLink peer stores, in two exchanges
+// that together are a reduce-scatter and an all-gather:
+//  1. every rank sends its partial of column h to the column's owner
+//     (owner = h / (H / world)) as 8-byte units {fp32 value, flag};
+//  2. the owner sums the `world` partials of each of its columns in rank
+//     order 0..world-1 (deterministic), writes the value to its own y and
+//     sends it to every other rank as units {fp32, flag};
+//  3. every rank copies the other ranks' columns into its y.
+// A unit's flag is the call count | 2^31, stored with the value as one
+// 64-bit access, so a reader that sees the flag sees the value; two slots
+// alternate by call parity and the last CTA advances the call count, as in
+// the gathered dense GEMV.  Waits are bounded (kWaitLimitNs); a rank that
+// never arrives makes them give up with kDevErrPeerTimeout.  Step 1 has no
+// waits and every CTA finishes it before it waits, and the grid (at most one
+// CTA per SM, nothing else running) is co-resident, so the waits cannot
+// cycle.
+//
+// Exchange buffer of a rank (moe_ep_xchg_bytes): a 256-byte control block
+// (word 0: calls completed, word 1: CTA count of the running call) and two
+// slots of [world][max_tokens][H / world] partial units followed by
+// [max_tokens][H] result units.
+struct MoeEp {
+  uint8_t* const* peers;
+  int rank, world;
+  int64_t max_tokens;
+};
+constexpr int64_t kMoeEpCtrlBytes = 256;
+__host__ __device__ constexpr int64_t moe_ep_slot_bytes(int64_t max_tokens, int64_t H) { return 16 * max_tokens * H; }
+
+__device__ __forceinline__ void st_unit_sys(uint8_t* dst, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_unit_sys(const uint8_t* src) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(src) : "memory");
+  return v;
+}
+// Bounded poll for a unit carrying `flag`; false (and the device error) on
+// giving up.
+__device__ __forceinline__ bool wait_unit(const uint8_t* src, uint32_t flag, uint64_t& v) {
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    v = ld_unit_sys(src);
+    if (static_cast<uint32_t>(v >> 32) == flag) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_device_error(kDevErrPeerTimeout);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void moe_store_y(const MoeArgs& a, int64_t t, int64_t h, float v) {
+  const int64_t off = t * a.y_stride + h;
+  if (a.y_bf16) {
+    static_cast<uint16_t*>(a.y)[off] = static_cast<uint16_t>(pack_bf16x2(v, 0.f) & 0xFFFFu);
+  } else if (a.accumulate) {
+    static_cast<float*>(a.y)[off] += v;
+  } else {
+    static_cast<float*>(a.y)[off] = v;
+  }
+}
+
+__global__ void __launch_bounds__(512) moe_ep_combine(const MoeArgs a, const MoeEp ep) {
+  // every CTA is running before a dependent grid may start (co-residency)
+  griddep_launch_dependents();
+  griddep_wait();
+  const float* part = reinterpret_cast<const float*>(a.ws + a.L.part);
+  const int64_t T = a.T, H = a.H, Hs = H / ep.world;
+  uint8_t* own = ep.peers[ep.rank];
+  const uint32_t calls = *reinterpret_cast<volatile const uint32_t*>(own);
+  const uint32_t flag = calls | 0x80000000u;
+  const uint64_t hi = static_cast<uint64_t>(flag) << 32;
+  const int64_t slot_off = kMoeEpCtrlBytes + (calls & 1) * moe_ep_slot_bytes(ep.max_tokens, H);
+  const int64_t part_region = static_cast<int64_t>(ep.world) * ep.max_tokens * Hs * 8;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  // a rank that failed to arrive earlier leaves the call counts disagreeing:
+  // skip the waits until the host has read the error
+  bool ok = !(*(volatile uint32_t*)&g_device_error & kDevErrPeerTimeout);
+  // 1. this rank's partials, to each column's owner
+  for (int64_t e = tid; e < T * H; e += stride) {
+    const int64_t t = e / H, h = e - t * H;
+    float sum = 0.f;
+    for (int j = 0; j < a.topk; ++j) {
+      const int pair = static_cast<int>(t) * a.topk + j;
+      const int ex = a.ids[pair] - a.e0;
+      if (ex >= 0 && ex < a.E_local) sum += part[static_cast<int64_t>(pair) * H + h];
+    }
+    const int q = static_cast<int>(h / Hs);
+    st_unit_sys(ep.peers[q] + slot_off + ((static_cast<int64_t>(ep.rank) * ep.max_tokens + t) * Hs + (h - q * Hs)) * 8,
+                hi | __float_as_uint(sum));
+  }
+  // 2. this rank's columns: every rank's partial, summed in rank order
+  for (int64_t e = tid; ok && e < T * Hs; e += stride) {
+    const int64_t t = e / Hs, hl = e - t * Hs;
+    float sum = 0.f;
+    for (int r = 0; r < ep.world && ok; ++r) {
+      uint64_t v;
+      ok = wait_unit(own + slot_off + ((static_cast<int64_t>(r) * ep.max_tokens + t) * Hs + hl) * 8, flag, v);
+      sum += __uint_as_float(static_cast<uint32_t>(v));
+    }
+    if (!ok) break;
+    const int64_t h = static_cast<int64_t>(ep.rank) * Hs + hl;
+    moe_store_y(a, t, h, sum);
+    for (int r = 0; r < ep.world; ++r)
+      if (r != ep.rank) st_unit_sys(ep.peers[r] + slot_off + part_region + (t * H + h) * 8, hi | __float_as_uint(sum));
+  }
+  // 3. the other ranks' columns
+  for (int64_t e = tid; ok && e < T * H; e += stride) {
+    const int64_t t = e / H, h = e - t * H;
+    if (h / Hs == ep.rank) continue;
+    uint64_t v;
+    ok = wait_unit(own + slot_off + part_region + (t * H + h) * 8, flag, v);
+    if (ok) moe_store_y(a, t, h, __uint_as_float(static_cast<uint32_t>(v)));
+  }
+  // the last CTA to finish advances the call count (every CTA read it above;
+  // the next call's CTAs read it only after this grid has completed)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* ctrl = reinterpret_cast<uint32_t*>(own);
+    uint32_t before;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(before) : "l"(ctrl + 1) : "memory");
+    if (before == gridDim.x - 1) {
+      ctrl[1] = 0u;
+      ctrl[0] = calls + 1u;
+    }
+  }
+}
+
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, void** args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -466,7 +601,7 @@ cudaError_t launch_moe_gemv(const MoeArgs& a, cudaStream_t stream) {
 }
 
 template <int FMT>
-cudaError_t moe_run(const MoeArgs& a, cudaStream_t stream) {
+cudaError_t moe_run(const MoeArgs& a, cudaStream_t stream, const MoeEp* ep = nullptr) {
   MoeArgs args = a;
   {
     void* kargs[] = {&args};
@@ -480,6 +615,13 @@ cudaError_t moe_run(const MoeArgs& a, cudaStream_t stream) {
   e = launch_moe_gemv<FMT, 2>(a, stream);
   if (e != cudaSuccess) return e;
   const int64_t total = static_cast<int64_t>(a.T) * a.H;
+  if (ep != nullptr) {
+    // persistent and co-resident: at most one CTA per SM
+    MoeEp epa = *ep;
+    const int blocks = static_cast<int>(std::min<int64_t>((total + 511) / 512, int64_t(device_sm_count())));
+    void* kargs[] = {&args, &epa};
+    return launch_pdl(reinterpret_cast<const void*>(moe_ep_combine), dim3(blocks), dim3(512), 0, stream, kargs);
+  }
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, int64_t(device_sm_count()) * 8));
   void* kargs[] = {&args};
   return launch_pdl(reinterpret_cast<const void*>(moe_combine), dim3(blocks), dim3(256), 0, stream, kargs);
@@ -500,10 +642,11 @@ bool moe_shape_ok(int fmt, int64_t H, int64_t I) {
   return H <= 4096 && I <= 2048;
 }
 
-cudaError_t moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w_down, const void* x,
-                    int64_t x_stride, const int32_t* ids, const float* wts, void* y, int64_t y_stride, bool y_bf16,
-                    bool accumulate, bool ftz, int64_t T, int64_t topk, int64_t H, int64_t I, int64_t e0,
-                    int64_t E_local, void* ws, cudaStream_t stream) {
+namespace {
+
+MoeArgs moe_args(int fmt, const void* w_gate, const void* w_up, const void* w_down, const void* x, int64_t x_stride,
+                 const int32_t* ids, const float* wts, void* y, int64_t y_stride, bool y_bf16, bool accumulate,
+                 bool ftz, int64_t T, int64_t topk, int64_t H, int64_t I, int64_t e0, int64_t E_local, void* ws) {
   MoeArgs a{};
   a.fmt = fmt;
   a.w_gate = static_cast<const uint8_t*>(w_gate);
@@ -529,12 +672,42 @@ cudaError_t moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w
   a.E_local = static_cast<int>(E_local);
   a.ws = static_cast<uint8_t*>(ws);
   a.L = moe_layout(E_local, H, I, T, topk);
-  switch (fmt) {
-    case kQ4_0: return moe_run<kQ4_0>(a, stream);
-    case kQ8_0: return moe_run<kQ8_0>(a, stream);
-    case kQ6_K: return moe_run<kQ6_K>(a, stream);
+  return a;
+}
+
+cudaError_t moe_dispatch(const MoeArgs& a, cudaStream_t stream, const MoeEp* ep) {
+  switch (a.fmt) {
+    case kQ4_0: return moe_run<kQ4_0>(a, stream, ep);
+    case kQ8_0: return moe_run<kQ8_0>(a, stream, ep);
+    case kQ6_K: return moe_run<kQ6_K>(a, stream, ep);
   }
   return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+cudaError_t moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w_down, const void* x,
+                    int64_t x_stride, const int32_t* ids, const float* wts, void* y, int64_t y_stride, bool y_bf16,
+                    bool accumulate, bool ftz, int64_t T, int64_t topk, int64_t H, int64_t I, int64_t e0,
+                    int64_t E_local, void* ws, cudaStream_t stream) {
+  return moe_dispatch(moe_args(fmt, w_gate, w_up, w_down, x, x_stride, ids, wts, y, y_stride, y_bf16, accumulate,
+                               ftz, T, topk, H, I, e0, E_local, ws),
+                      stream, nullptr);
+}
+
+int64_t moe_ep_xchg_bytes(int64_t H, int64_t max_tokens) {
+  return kMoeEpCtrlBytes + 2 * moe_ep_slot_bytes(max_tokens, H);
+}
+
+cudaError_t moe_ffn_ep(int fmt, const void* w_gate, const void* w_up, const void* w_down, const void* x,
+                       int64_t x_stride, const int32_t* ids, const float* wts, void* y, int64_t y_stride, bool y_bf16,
+                       bool accumulate, bool ftz, int64_t T, int64_t topk, int64_t H, int64_t I, int64_t e0,
+                       int64_t E_local, void* ws, uint8_t* const* peers, int rank, int world, int64_t max_tokens,
+                       cudaStream_t stream) {
+  const MoeEp ep{peers, rank, world, max_tokens};
+  return moe_dispatch(moe_args(fmt, w_gate, w_up, w_down, x, x_stride, ids, wts, y, y_stride, y_bf16, accumulate,
+                               ftz, T, topk, H, I, e0, E_local, ws),
+                      stream, &ep);
 }
 
 // ------------------------------------------------ allocation-free variant ----

@@ -128,3 +128,27 @@ class AllGatherExchange:
         self.peers = torch.tensor(list(self._hdl.buffer_ptrs), dtype=torch.int64, device=device)
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
+
+
+class MoeExchange:
+    """Exchange buffers for spiral_b200.moe_ffn_ep (expert-parallel MoE) for
+    up to max_tokens tokens of width `hidden`: one symmetric-memory
+    allocation per rank, zeroed, and the device array of every rank's
+    pointer (``peers``).  Collective: every rank constructs it with the same
+    arguments."""
+
+    def __init__(self, hidden: int, max_tokens: int, device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import moe_ep_exchange_bytes
+
+        nbytes = moe_ep_exchange_bytes(hidden, max_tokens)
+        if nbytes <= 0:
+            raise ValueError("hidden and max_tokens must be positive")
+        self.hidden, self.max_tokens = hidden, max_tokens
+        self._buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
+        self._buf.zero_()
+        self._hdl = symm_mem.rendezvous(self._buf, group=group if group is not None else dist.group.WORLD)
+        self.peers = torch.tensor(list(self._hdl.buffer_ptrs), dtype=torch.int64, device=device)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)

@@ -195,3 +195,67 @@ def test_mul_mat_allgather_validation_codes():
     assert call(off=7164, N=7172) == -4  # 8-column granularity
     assert call(ys=14340) == -4
     assert call(y=264) == -4
+
+
+def test_repack_rejects_misaligned_input_with_zero():
+    # odd addresses or strides (the device repack moves 2-byte granules)
+    assert sp.repack(sp.Q4_0, 17, 2304, 32, 1 << 20, 4096, 8) == 0
+    assert sp.repack(sp.Q4_0, 16, 2305, 32, 1 << 20, 4096, 8) == 0
+    assert sp.repack(sp.Q4_0, 16, 2304, 33, 1 << 20, 4096, 8) == 0
+
+
+def test_repack_warning_hook_is_settable_without_a_gpu():
+    lines = []
+    sp.set_repack_warn(lines.append)
+    sp.set_repack_warn(None)
+    sp.set_repack_warn(to_stderr=True)
+    assert lines == []
+
+
+def test_moe_ep_validates_its_arguments():
+    """Host-side argument checks of spiral_moe_ffn_ep (nothing is launched)."""
+    L = sp.lib()
+    p = 256  # never dereferenced: every case fails validation first
+    H, I, E, topk = 2048, 768, 8, 8
+    args = dict(fmt=sp.Q4_0, E=E, e0=0, H=H, I=I, T=4, maxT=4, topk=topk, peers=p, rank=0, world=2, ws=1 << 30)
+
+    def call(**kw):
+        a = dict(args, **kw)
+        return L.spiral_moe_ffn_ep(a["fmt"], p, p, p, a["E"], a["e0"], a["H"], a["I"], p, H, a["T"], a["maxT"], p,
+                                   p, a["topk"], p, sp.BF16, H, a["peers"], a["rank"], a["world"], p, a["ws"], 0, 0)
+
+    assert call(rank=2) == -10
+    assert call(world=0) == -10
+    assert call(peers=0) == -3
+    assert call(T=5) == -5  # more tokens than the exchange holds
+    assert call(H=2048, world=3) == -2  # hidden not a multiple of world
+    assert sp.moe_ep_exchange_bytes(0, 4) == 0 and sp.moe_ep_exchange_bytes(H, 4) > 0
+
+
+def test_ggml_supports_mul_mat_follows_ggml_rules():
+    """supports_op for GGML_OP_MUL_MAT (host logic only; nothing launched)."""
+    K, N, M = 4096, 64, 2
+    p = 256
+
+    def node(t0=sp.Q4_0, t1=sp.BF16, td=sp.F32, k1=K, ne12=1, ne02=1, nb00=None, nb10=2):
+        bb, bk = sp.BLOCK_BYTES.get(t0, 18), sp.BLOCK_K.get(t0, 32)
+        rb = K // bk * bb
+        src0 = sp.ggml_tensor(t0, (K, N, ne02, 1), (nb00 or bb, rb, rb * N, rb * N * ne02), p)
+        src1 = sp.ggml_tensor(t1, (k1, M, ne12, 1), (nb10, 2 * k1, 2 * k1 * M, 2 * k1 * M * ne12), p)
+        es = 4 if td == sp.F32 else 2
+        dst = sp.ggml_tensor(td, (N, M, ne12, 1), (es, es * N, es * N * M, es * N * M * ne12), p)
+        return src0, src1, dst
+
+    assert sp.ggml_supports_mul_mat(*node())
+    for t0 in (sp.Q8_0, sp.Q6_K):
+        assert sp.ggml_supports_mul_mat(*node(t0=t0))
+    assert sp.ggml_supports_mul_mat(*node(td=sp.BF16))
+    assert sp.ggml_supports_mul_mat(*node(ne12=4, ne02=2))  # broadcast
+    assert not sp.ggml_supports_mul_mat(*node(ne12=3, ne02=2))  # not a multiple
+    assert not sp.ggml_supports_mul_mat(*node(t0=0))  # F32 src0: not quantized
+    assert not sp.ggml_supports_mul_mat(*node(t1=0))  # F32 src1
+    assert not sp.ggml_supports_mul_mat(*node(k1=K - 32))  # K mismatch
+    assert not sp.ggml_supports_mul_mat(*node(nb10=4))  # non-contiguous src1 rows
+    assert not sp.ggml_supports_mul_mat(*node(nb00=36))  # strided blocks
+    s0, s1, d = node(t1=0)
+    assert sp.lib().spiral_ggml_mul_mat(ctypes.byref(s0), ctypes.byref(s1), ctypes.byref(d), 0, 0) == -9

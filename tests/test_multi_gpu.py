@@ -1,8 +1,17 @@
-"""Multi-GPU paths on 2 B200s (skipped with fewer GPUs): the row-sharded
-dequant-GEMV with an NCCL all-gather and with the all-gather fused into the
-kernel (NVLink peer stores), and the expert-parallel MoE layer with
-NCCL all-to-all dispatch and combine, each rank running libspiral_b200 on its
-own GPU.  Checked against the float64 oracle of the whole operation."""
+"""Multi-GPU paths on min(8, visible) B200s (skipped with fewer than 2): every
+rank is a process with its own GPU running libspiral_b200.
+
+* dense row-sharded MUL_MAT (BASELINE config 2 dims, 14336 x 4096 Q4_0):
+  NCCL all-gather, and the all-gather fused into the GEMV (flagged NVLink
+  units): equal bit for bit to spiral_mul_mat on the whole weight, on every
+  rank, for B = 1, 2, 5, 8 and several calls through one exchange; checked
+  against the float64 oracle once;
+* expert-parallel MoE layer (BASELINE config 4 dims: 128 Q4_0 experts,
+  hidden 2048, inter 768, top-8, T = 1 and 64) through spiral_moe_ffn_ep
+  (combine fused over NVLink): identical on every rank and within the MoE
+  tolerance of the float64 oracle of the whole layer;
+* the Python NCCL all-to-all dispatch/combine (spiral_b200.dist) at toy dims.
+"""
 
 from __future__ import annotations
 
@@ -28,6 +37,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def _bits(t):
+    import torch
+
+    return t.contiguous().view(torch.int16 if t.element_size() == 2 else torch.int32)
+
+
 def _worker(rank, world, port, q):
     import torch
     import torch.distributed as dist
@@ -35,54 +50,92 @@ def _worker(rank, world, port, q):
     import oracle
     import spiral_b200 as sp
     from oracle import formats as F
-    from spiral_b200.dist import expert_range, gather_rows, moe_dispatch_combine, row_range
+    from spiral_b200.dist import AllGatherExchange, MoeExchange, expert_range, gather_rows, moe_dispatch_combine, row_range
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    res = {"rank": rank}
     try:
         from tests.gpu_util import tolerance_ok
 
-        # dense: Q4_0 14336 x 4096, B = 4, row-sharded
-        fid, K, N, M = F.Q4_0, 4096, 1792, 4
+        fid, K = F.Q4_0, 4096
+        rb = F.row_bytes(fid, K)
+
+        # dense, NCCL all-gather after the shard GEMV
+        N, M = 1792, 4
         raw = F.generate(fid, K, N, seed=3)
         x = F.gen_activations(M, K, seed=4)
         n0, n1 = row_range(N, world, rank)
-        rb = F.row_bytes(fid, K)
         w = torch.from_numpy(raw[n0 * rb:n1 * rb]).to(dev)
         xd = torch.from_numpy(x.view(np.int16)).to(dev).view(torch.bfloat16)
         y_local = sp.mul_mat(fid, w, xd, n1 - n0, K, y_dtype=sp.F32, static_weights=True)
         y = gather_rows(y_local, N).cpu().numpy()
-        ok_dense, rel_dense = tolerance_ok(y, oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=False)
+        res["dense_nccl"] = tolerance_ok(y, oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=False)
 
-        # the same GEMV with the all-gather fused in (flagged units over
-        # NVLink), uneven shards (113 tiles of 16 rows over 2 ranks), every
-        # batch size, one output per batch size, several calls in a row
-        # through one exchange
-        from spiral_b200.dist import AllGatherExchange
-
-        Ng = 1808
+        # dense, all-gather fused in: config 2 dims, bitwise vs the whole weight
+        Ng = 14336
         rawg = F.generate(fid, K, Ng, seed=7)
         g0, g1 = row_range(Ng, world, rank)
         wg_shard = torch.from_numpy(rawg[g0 * rb:g1 * rb]).to(dev)
+        wg_full = torch.from_numpy(rawg).to(dev)
         xc = AllGatherExchange(Ng, dev)
         outs = {B: torch.zeros((B, Ng), dtype=torch.bfloat16, device=dev) for B in (1, 2, 5, 8)}
-        ok_fused, rel_fused = True, 0.0
+        mism, rel_max = 0, 0.0
         for it in range(7):
             B = (1, 2, 5, 8)[it % 4]
             xb = F.gen_activations(B, K, seed=20 + it)
             xdb = torch.from_numpy(xb.view(np.int16)).to(dev).view(torch.bfloat16)
             sp.mul_mat_allgather(fid, wg_shard, xdb, g1 - g0, K, outs[B], g0, xc.peers, rank, world)
-            yg = outs[B].float().cpu().numpy()
-            ok, rel = tolerance_ok(yg, oracle.mul_mat_f64(fid, rawg, xb, K, Ng), bf16_out=True)
-            ok_fused, rel_fused = ok_fused and ok, max(rel_fused, rel)
+            want = sp.mul_mat(fid, wg_full, xdb, Ng, K, y_dtype=sp.BF16)
+            mism += int((_bits(outs[B]) != _bits(want)).sum().item())
+            if it == 3 and rank == 0:
+                ok, rel = tolerance_ok(outs[B].float().cpu().numpy(), oracle.mul_mat_f64(fid, rawg, xb, K, Ng),
+                                       bf16_out=True)
+                res["fused_oracle"] = (ok, rel)
+        res["fused_mismatch"] = mism
         torch.cuda.synchronize()
         dist.barrier()
         del xc
 
-        # MoE: 16 Q4_0 experts, hidden 512, inter 256, top-4, tokens sharded
+        # expert-parallel MoE at config 4 dims through spiral_moe_ffn_ep
+        E, H, I, topk = 128, 2048, 768, 8
+        e0, e1 = expert_range(E, world, rank)
+        gu, dd = I * F.row_bytes(fid, H), H * F.row_bytes(fid, I)
+        # experts are generated per expert id, so every rank builds only its own
+        wg_l = torch.from_numpy(np.concatenate([F.generate(fid, H, I, seed=11000 + e) for e in range(e0, e1)])).to(dev)
+        wu_l = torch.from_numpy(np.concatenate([F.generate(fid, H, I, seed=12000 + e) for e in range(e0, e1)])).to(dev)
+        wd_l = torch.from_numpy(np.concatenate([F.generate(fid, I, H, seed=13000 + e) for e in range(e0, e1)])).to(dev)
+        mx = MoeExchange(H, 64, dev)
+        for T in (1, 64, 1):
+            xm = F.gen_activations(T, H, seed=500 + T)
+            ids, wts = F.gen_routing(T, E, topk, seed=600 + T)
+            xmd = torch.from_numpy(xm.view(np.int16)).to(dev).view(torch.bfloat16).view(T, H)
+            y = sp.moe_ffn_ep(fid, wg_l, wu_l, wd_l, xmd, torch.from_numpy(ids).to(dev),
+                              torch.from_numpy(wts).to(dev), hidden=H, inter=I, n_experts_local=e1 - e0,
+                              expert_first=e0, exchange_peers_dev=mx.peers, rank=rank, world=world, max_tokens=64,
+                              y_dtype=sp.F32)
+            torch.cuda.synchronize()
+            allys = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(allys, y)
+            res[f"ep_identical_T{T}"] = all(torch.equal(_bits(allys[0]), _bits(a)) for a in allys)
+            if rank == 0 and f"ep_oracle_T{T}" not in res:
+                used = sorted(set(int(v) for v in ids.reshape(-1)))
+                if "all_experts" not in res:  # the whole layer's experts, once (host only)
+                    res["all_experts"] = tuple(np.concatenate([F.generate(fid, k, n, seed=s0 + e) for e in range(E)])
+                                               for s0, k, n in ((11000, H, I), (12000, H, I), (13000, I, H)))
+                ref = oracle.moe_ffn_f64(fid, *res["all_experts"], xm, ids, wts, H, I, E)
+                res[f"ep_oracle_T{T}"] = tolerance_ok(y.cpu().numpy(), ref, bf16_out=False, rel_tol=2e-3)
+                res[f"ep_experts_T{T}"] = len(used)
+        res.pop("all_experts", None)
+        torch.cuda.synchronize()
+        dist.barrier()
+        del mx
+
+        # Python NCCL all-to-all dispatch/combine over spiral_moe_ffn (toy dims)
         E, H, I, T, topk = 16, 512, 256, 9, 4
         wg = F.gen_experts(fid, E, I, H, seed=1)
         wu = F.gen_experts(fid, E, I, H, seed=2)
@@ -104,27 +157,36 @@ def _worker(rank, world, port, q):
                                   torch.from_numpy(ids[t0:t1]).to(dev), torch.from_numpy(wts[t0:t1]).to(dev), E,
                                   compute)
         ref = oracle.moe_ffn_f64(fid, wg, wu, wdn, xm, ids, wts, H, I, E)[t0:t1]
-        ok_moe, rel_moe = tolerance_ok(ym.cpu().numpy(), ref, bf16_out=False, rel_tol=2e-3)
-        q.put((rank, ok_dense, rel_dense, ok_moe, rel_moe, ok_fused, rel_fused, sp.device_status()))
+        res["a2a"] = tolerance_ok(ym.cpu().numpy(), ref, bf16_out=False, rel_tol=2e-3)
+        res["status"] = sp.device_status()
+        q.put(res)
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
-def test_two_gpu_row_shard_and_expert_parallel_moe():
+def test_multi_gpu_row_shard_and_expert_parallel_moe():
     import torch.multiprocessing as mp
 
+    world = min(8, _ngpu())
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=300)
-    assert [p.exitcode for p in procs] == [0, 0]
-    for rank, ok_d, rel_d, ok_m, rel_m, ok_f, rel_f, status in (q.get() for _ in range(2)):
-        assert ok_d, (rank, rel_d)
-        assert ok_f, (rank, rel_f)
-        assert ok_m, (rank, rel_m)
-        assert status == 0
+        p.join(timeout=600)
+    assert [p.exitcode for p in procs] == [0] * world
+    results = [q.get() for _ in range(world)]
+    for r in results:
+        assert r["dense_nccl"][0], r
+        assert r["fused_mismatch"] == 0, r
+        assert r["a2a"][0], r
+        for T in (1, 64):
+            assert r[f"ep_identical_T{T}"], r
+        assert r["status"] == 0, r
+    r0 = next(r for r in results if r["rank"] == 0)
+    assert r0["fused_oracle"][0], r0
+    for T in (1, 64):
+        assert r0[f"ep_oracle_T{T}"][0], r0
