@@ -904,6 +904,25 @@ def bench_extras(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, tc_peak,
                     "roofline": roofline("hbm", alg, t, hbm_peak, peak_kind, f"gemv_kernel<{name}>",
                                          profile_traffic(f"gemv_{name}_K{K}_N{N}_B{B}"))}
             del ws, w0
+        # model shape (Gemma-style Q6_K output head, K = 1536, 262,144 rows:
+        # 330 MB, larger than L2 on its own)
+        fid, Kh, Nh = F.Q6_K, 1536, 262144
+        rbh = F.row_bytes(fid, Kh)
+        wh = torch.from_numpy(F.generate(fid, Kh, Nh, seed=0)).to(dev)
+        for B in (1, 8):
+            x = torch.from_numpy(F.gen_activations(B, Kh, seed=B).view(np.int16)).to(dev).view(torch.bfloat16)
+            y = torch.empty((B, Nh), dtype=torch.bfloat16, device=dev)
+
+            def body_h(i, x=x, y=y):
+                sp.mul_mat(fid, wh, x, Nh, Kh, y, y_dtype=sp.BF16, static_weights=True)
+
+            t = timer.timed(8, 3, body_h, gsteps=4) / 8 * 1e-3
+            alg = rbh * Nh + B * Kh * 2 + B * Nh * 2
+            out["gemv"][f"q6_k_K{Kh}_N{Nh}_B{B}"] = {
+                "us": t * 1e6, "weight_GBps": rbh * Nh / t / 1e9,
+                "roofline": roofline("hbm", alg, t, hbm_peak, peak_kind, "gemv_kernel<q6_k> (window rows)",
+                                     profile_traffic(f"gemv_q6_k_K{Kh}_N{Nh}_B{B}"))}
+        del wh
     out["dequant"] = bench_dequant(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_kind)
     out["gemm"] = bench_gemm(sp, F, dev, rank, world, timer, hbm_peak, tc_peak, peak_kind)
     out["moe"] = bench_moe(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_kind)

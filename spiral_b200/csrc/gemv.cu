@@ -72,6 +72,12 @@ struct GemvParams {
   int x_pitch;    // bytes per activation vector in the permuted copy
   int y_bf16, accumulate, ftz;
   int static_weights;  // weights may be read before the preceding grid ends
+  // Rows whose address or stride is not 16-byte aligned (e.g. Q6_K at
+  // K = 1536: 1260-byte rows): each row is copied as the 16-byte aligned
+  // window that holds it, and read at its offset inside the window.  The
+  // window's extra bytes lie in the same 16-byte granules as the row's first
+  // and last bytes, so they never reach another page.
+  int window;
   // Gathered output (world > 0): y is this rank's full bf16 output
   // [M][y_sm]; the shard's rows are columns n_offset + n of it, and every
   // rank's exchange buffer (xchg_peers[r]) receives them as flagged units.
@@ -219,10 +225,25 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
           const int64_t g0 = static_cast<int64_t>(ch) * p.chunk_groups;
           const int ng = static_cast<int>(::spiral::min64(p.chunk_groups, p.groups_per_row - g0));
           const uint32_t bytes = static_cast<uint32_t>(ng * F::kGroupBytes);
-          mbar_arrive_expect_tx(&full[s], bytes * rows);
           uint8_t* dst = stages + s * stage_bytes;
           const uint8_t* src = src_tile + g0 * F::kGroupBytes;
-          for (int r = 0; r < rows; ++r) bulk_g2s(dst + r * p.row_pitch, src + r * p.w_stride, bytes, &full[s], pol);
+          if (p.window) {
+            uint32_t total = 0;
+            for (int r = 0; r < rows; ++r) {
+              const uint32_t off = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(src + r * p.w_stride) & 15u);
+              total += (off + bytes + 15u) & ~15u;
+            }
+            mbar_arrive_expect_tx(&full[s], total);
+            for (int r = 0; r < rows; ++r) {
+              const uint8_t* row = src + r * p.w_stride;
+              const uint32_t off = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row) & 15u);
+              bulk_g2s(dst + r * p.row_pitch, row - off, (off + bytes + 15u) & ~15u, &full[s], pol);
+            }
+          } else {
+            mbar_arrive_expect_tx(&full[s], bytes * rows);
+            for (int r = 0; r < rows; ++r)
+              bulk_g2s(dst + r * p.row_pitch, src + r * p.w_stride, bytes, &full[s], pol);
+          }
         }
       }
     drain:
@@ -265,6 +286,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         const uint8_t* st = stages + s * stage_bytes;
         const uint8_t* ra = st + r * p.row_pitch;
         const uint8_t* rb = st + (r + 8) * p.row_pitch;
+        if (p.window) {  // the row's offset inside its window (rows past N: any)
+          const uint8_t* row0 = p.w + tile * kTileRows * p.w_stride;
+          ra += reinterpret_cast<uintptr_t>(row0 + r * p.w_stride) & 15u;
+          rb += reinterpret_cast<uintptr_t>(row0 + (r + 8) * p.w_stride) & 15u;
+        }
         auto decode = [&](int gl) {
           const uint8_t* xg = xcol + (g0 + gl) * F::kSteps * 32;
           if constexpr (FMT == kQ6_K) {
@@ -447,6 +473,7 @@ __global__ void __launch_bounds__(256) gemv_generic(const MatArgs a) {
 
 struct GemvPlan {
   int chunk_groups = 0, chunks = 0, stages = 0, row_pitch = 0, x_pitch = 0;
+  bool window = false;
   size_t smem = 0;
 };
 
@@ -457,7 +484,27 @@ static bool gemv_plan(const MatArgs& a, GemvPlan* out) {
   using F = GemvFmt<FMT>;
   if (a.M < 1 || a.M > 8) return false;
   const int64_t gpr = a.K / F::kGroupK;
-  if (a.K % (static_cast<int64_t>(F::kGroupK) * F::kChunkAlign) != 0) return false;
+  if (a.K % F::kGroupK != 0) return false;
+  const bool aligned = reinterpret_cast<uintptr_t>(a.w) % 16 == 0 && a.w_stride % 16 == 0;
+  if (!aligned || a.K % (static_cast<int64_t>(F::kGroupK) * F::kChunkAlign) != 0) {
+    // window copies: whole rows only, each starting 4-byte aligned (the
+    // decoders' alignment); the window holds up to 15 bytes around the row
+    if (reinterpret_cast<uintptr_t>(a.w) % 4 != 0 || a.w_stride % 4 != 0) return false;
+    const size_t avail = device_max_smem_optin();
+    const int64_t x_pitch = a.K * 2 + 32;
+    const size_t fixed = kBarrierBytes + kRedBytes + static_cast<size_t>(a.M) * x_pitch;
+    const int64_t pitch = ((gpr * F::kGroupBytes + 15 + 15) / 16) * 16 + 16;
+    const int64_t stage = kTileRows * pitch;
+    if (fixed >= avail || static_cast<int64_t>(avail - fixed) / stage < 2) return false;
+    out->chunk_groups = static_cast<int>(gpr);
+    out->chunks = 1;
+    out->stages = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(avail - fixed) / stage, F::kMaxStages));
+    out->row_pitch = static_cast<int>(pitch);
+    out->x_pitch = static_cast<int>(x_pitch);
+    out->smem = fixed + static_cast<size_t>(out->stages) * stage;
+    out->window = true;
+    return true;
+  }
   const size_t avail = device_max_smem_optin();
   const int64_t x_pitch = a.K * 2 + 32;
   const size_t fixed = kBarrierBytes + kRedBytes + static_cast<size_t>(a.M) * x_pitch;
@@ -486,7 +533,6 @@ static bool gemv_plan(const MatArgs& a, GemvPlan* out) {
 
 template <int FMT>
 static bool gemv_fast_ok_t(const MatArgs& a) {
-  if (reinterpret_cast<uintptr_t>(a.w) % 16 != 0 || a.w_stride % 16 != 0) return false;
   GemvPlan plan;
   return gemv_plan<FMT>(a, &plan);
 }
@@ -505,7 +551,7 @@ static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream, const PeerOut* 
   using F = GemvFmt<FMT>;
   if (gemv_xs_ok(a)) return gemv_xs(a, po, stream);
   GemvPlan plan;
-  if (reinterpret_cast<uintptr_t>(a.w) % 16 != 0 || a.w_stride % 16 != 0 || !gemv_plan<FMT>(a, &plan)) {
+  if (!gemv_plan<FMT>(a, &plan) || (po != nullptr && plan.window)) {
     if (po != nullptr) return cudaErrorNotSupported;
     const int64_t blocks = std::min<int64_t>((a.N + 7) / 8, int64_t(device_sm_count()) * 16);
     gemv_generic<FMT><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
@@ -533,6 +579,7 @@ static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream, const PeerOut* 
   p.accumulate = a.accumulate;
   p.ftz = a.ftz;
   p.static_weights = a.static_weights;
+  p.window = plan.window;
   if (po != nullptr) {
     p.xchg_peers = po->xchg_peers;
     p.n_offset = po->n_offset;

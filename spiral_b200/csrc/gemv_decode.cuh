@@ -21,13 +21,13 @@ template <int FMT> struct GemvFmt;
 // k-steps per group; a chunk must be a multiple of kChunkAlign groups to stay
 // 16-byte aligned.
 template <> struct GemvFmt<kQ4_0> {
-  static constexpr int kGroupK = 128, kGroupBytes = 72, kSteps = 8, kChunkAlign = 2, kMaxStages = 4;
+  static constexpr int kGroupK = 128, kGroupBytes = 72, kSteps = 8, kChunkAlign = 2, kMaxStages = 8;
 };
 template <> struct GemvFmt<kQ8_0> {
-  static constexpr int kGroupK = 128, kGroupBytes = 136, kSteps = 8, kChunkAlign = 2, kMaxStages = 4;
+  static constexpr int kGroupK = 128, kGroupBytes = 136, kSteps = 8, kChunkAlign = 2, kMaxStages = 8;
 };
 template <> struct GemvFmt<kQ6_K> {
-  static constexpr int kGroupK = 256, kGroupBytes = 210, kSteps = 16, kChunkAlign = 8, kMaxStages = 4;
+  static constexpr int kGroupK = 256, kGroupBytes = 210, kSteps = 16, kChunkAlign = 8, kMaxStages = 8;
 };
 
 // ------------------------------------------------------------- helpers ---

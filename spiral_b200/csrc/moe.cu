@@ -46,8 +46,8 @@ constexpr int kMoeWarpsPerGroup = 8;
 constexpr int kMoeGroupThreads = kMoeWarpsPerGroup * 32;
 constexpr int kMoeConsumers = kMoeGroups * kMoeWarpsPerGroup;
 constexpr int kMoeThreads = (kMoeConsumers + 1) * 32;
-constexpr int kMoeMaxStages = 8;
-constexpr int kMoeBarrierBytes = 256;
+constexpr int kMoeMaxStages = 24;  // down-projection stages are small (16 rows x 432 B)
+constexpr int kMoeBarrierBytes = 512;  // 24 mbarrier pairs + the abort word
 constexpr int kRouteThreads = 1024;
 constexpr int kTileRows = 16;
 

@@ -83,7 +83,7 @@ def test_gemv_baseline_config2(cuda, big_weights, fid, M):
         (5, 37, 4096),  # ragged N (partial 16-row tile)
         (8, 4096, 4096),
         (2, 2048, 768),  # MoE down-projection K (partial chunk)
-        (3, 96, 1536),  # Gemma K: Q6_K generic path
+        (3, 96, 1536),  # Gemma K: Q6_K window copies
         (12, 64, 2048),  # M > 8: batched GEMV launches
     ],
 )
@@ -269,3 +269,33 @@ def test_gathered_gemv_single_rank(cuda, fid):
     del g
     assert xchg[:8].view(torch.int32).cpu().tolist() == [calls, 0]
     assert sp.device_status() == 0
+
+
+@pytest.mark.parametrize("M", [1, 8])
+def test_gemv_gemma_q6_k_output_head_shape(cuda, M):
+    """The Gemma-style Q6_K output head (K = 1536: 1260-byte rows, not a
+    16-byte multiple) runs the pipelined GEMV with window copies."""
+    fid, K, N = F.Q6_K, 1536, 4096
+    raw = F.generate(fid, K, N, seed=77)
+    x = F.gen_activations(M, K, seed=78)
+    y = sp.mul_mat(fid, dev_bytes(raw), dev_bf16(x), N, K, y_dtype=sp.F32).cpu().numpy()
+    ok, rel = tolerance_ok(y, oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=False)
+    assert ok, rel
+    assert rel < 1e-5, rel
+
+
+@pytest.mark.parametrize("fid", FMTS, ids=lambda f: F.NAMES[f])
+def test_gemv_rows_off_16_byte_alignment(cuda, fid):
+    """Rows at a stride that is 4 mod 16 (window copies) and at a 4-byte
+    offset base."""
+    from .gpu_util import strided_rows
+
+    K, N, M = 2048, 200, 3
+    raw = F.generate(fid, K, N, seed=31)
+    rb = F.row_bytes(fid, K)
+    stride = rb + 4
+    w = dev_bytes(strided_rows(raw, N, rb, stride), offset=4)
+    x = F.gen_activations(M, K, seed=32)
+    y = sp.mul_mat(fid, w, dev_bf16(x), N, K, y_dtype=sp.F32, w_row_stride=stride).cpu().numpy()
+    ok, rel = tolerance_ok(y, oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=False)
+    assert ok, rel
