@@ -112,6 +112,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// The same test, but the thread may be suspended by the hardware until the
+// phase completes or about `hint_ns` have passed: a waiting warp then issues
+// nothing, leaving the issue slots to the warps that are decoding.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -120,15 +133,17 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // Bounded wait on an mbarrier phase: gives up after kWaitLimitNs of device
 // time, records kDevErrMbarTimeout in the device error word and returns
-// false, so callers drain and exit instead of hanging the GPU.
+// false, so callers drain and exit instead of hanging the GPU.  Each test
+// may sleep up to kWaitSleepNs, so a waiting warp costs almost no issue slots.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint32_t kWaitSleepNs = 100000u;         // 100 us per suspended test
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
 #pragma unroll 1
-    for (int i = 0; i < 64; ++i) {
-      if (mbar_try_wait(bar, parity)) return true;
+    for (int i = 0; i < 4; ++i) {
+      if (mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
     }
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       raise_device_error(kDevErrMbarTimeout);

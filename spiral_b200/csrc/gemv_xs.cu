@@ -75,6 +75,16 @@ __host__ __device__ constexpr int xs_pair_step(int s) {
                       : FMT == kQ8_0 ? ((s & 1) == 0 ? s + 1 : -1) : (((s >> 2) & 1) == 0 ? s + 4 : -1);
 }
 
+// Bounded wait that gives up at once when another warp already gave up (the
+// abort word is read only when the phase is not complete yet).
+__device__ __forceinline__ bool xs_wait(uint64_t* bar, uint32_t parity, int& abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  if (*(volatile int*)&abort_flag) return false;
+  if (mbar_wait(bar, parity)) return true;
+  abort_flag = 1;
+  return false;
+}
+
 // Weight row of MMA row R of a tile.
 __device__ __forceinline__ int xs_weight_row(int R) { return R < 8 ? 2 * R : 2 * (R - 8) + 1; }
 
@@ -211,18 +221,16 @@ __global__ void __launch_bounds__(kXsThreads, 1) gemv_xs_kernel(const XsParams p
 
   const int red_set = warp / kXsReducerWarps;
   uint16_t* tile_out = reinterpret_cast<uint16_t*>(smem + 1024) + red_set * (8 * kXsRows);
-  int64_t local = 0;
-  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
-    const int s = static_cast<int>(local % p.stages);
+  // MMA row r = weight row 2r (pair r, first row); row r + 8 = 2r + 1
+  const uint8_t* ra0 = stages + r * p.pair_pitch + warp * GPW * F::kGroupBytes;
+  const int ntiles = static_cast<int>(tiles);
+  int stage = 0, red_turn = 0;
+  uint32_t phase = 0u;
+  for (int tile = blockIdx.x, local = 0; tile < ntiles; tile += gridDim.x, ++local) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    bool ready = false;
-    if (!*(volatile int*)&abort_flag) {
-      ready = mbar_wait(&full[s], static_cast<uint32_t>(local / p.stages) & 1u);
-      if (!ready) abort_flag = 1;
-    }
-    if (ready) {
-      // MMA row r = weight row 2r (pair r, first row); row r + 8 = 2r + 1
-      const uint8_t* ra = stages + s * stage_bytes + r * p.pair_pitch + warp * GPW * F::kGroupBytes;
+    const int s = stage;
+    if (xs_wait(&full[s], phase, abort_flag)) {
+      const uint8_t* ra = ra0 + s * stage_bytes;
       const uint8_t* rb = ra + p.row_bytes;
 #pragma unroll
       for (int g = 0; g < GPW; ++g) {
@@ -239,20 +247,22 @@ __global__ void __launch_bounds__(kXsThreads, 1) gemv_xs_kernel(const XsParams p
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+    if (++stage == p.stages) {
+      stage = 0;
+      phase ^= 1u;
+    }
 
     // hand the partial to this tile's reducers
-    const int rbuf = static_cast<int>(local & 1);
-    if (local >= 2 && !*(volatile int*)&abort_flag) {
-      if (!mbar_wait(&red_empty[rbuf], static_cast<uint32_t>((local >> 1) - 1) & 1u)) abort_flag = 1;
-    }
+    const int rbuf = local & 1;
+    if (local >= 2) xs_wait(&red_empty[rbuf], static_cast<uint32_t>((local >> 1) - 1) & 1u, abort_flag);
     red[(rbuf * kXsWarps + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
     mbar_arrive(&red_full[rbuf]);
-    if (static_cast<int>(local % kXsReducerSets) != red_set) continue;
+    const bool mine = red_turn == red_set;
+    if (++red_turn == kXsReducerSets) red_turn = 0;
+    if (!mine) continue;
 
     // --------------------------------------------------- reduction ----
-    if (!*(volatile int*)&abort_flag) {
-      if (!mbar_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u)) abort_flag = 1;
-    }
+    xs_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u, abort_flag);
     const int t = (warp % kXsReducerWarps) * 32 + lane;  // 0..127: one output each
     const int l = t >> 2, j = t & 3;
     const float* rp = reinterpret_cast<const float*>(red + rbuf * kXsWarps * 32 + l) + j;
@@ -262,14 +272,14 @@ __global__ void __launch_bounds__(kXsThreads, 1) gemv_xs_kernel(const XsParams p
     mbar_arrive(&red_empty[rbuf]);
     const int row = xs_weight_row((l >> 2) + 8 * (j >> 1));
     const int m = 2 * (l & 3) + (j & 1);
-    const int64_t n = tile * kXsRows + row;
+    const int64_t n = static_cast<int64_t>(tile) * kXsRows + row;
     if constexpr (GATHER) {
       // the tile's bf16 outputs, [m][16 rows], then 16-byte pieces to the
       // local output and flagged unit pairs to every other rank's slot
       const int bar = 1 + red_set;
       tile_out[m * kXsRows + row] = static_cast<uint16_t>(pack_bf16x2(sum, 0.f) & 0xFFFFu);
       named_bar_sync(bar, kXsReducerWarps * 32);
-      const int64_t r0 = tile * kXsRows;
+      const int64_t r0 = static_cast<int64_t>(tile) * kXsRows;
       const int local_items = p.M * 2;
       const int items = *(volatile int*)&abort_flag ? local_items : local_items + p.M * 4 * (p.world - 1);
       for (int q = t; q < items; q += kXsReducerWarps * 32) {
