@@ -449,6 +449,11 @@ class Timer:
         cache = {}
         self.prepare(warm, cache, body, gsteps)
         self.prepare(nsteps, cache, body, gsteps)
+        if self.world > 1:
+            # fused exchanges wait on the device for at most 2 s: ranks start
+            # the warm-up together
+            torch.cuda.synchronize()
+            dist.barrier()
         with torch.cuda.stream(self.stream):
             self.replay(warm, cache, gsteps)
         torch.cuda.synchronize()
@@ -561,6 +566,8 @@ def run_spiral(args):
             mul_mat_full(weights[(i * len(BATCHES) + j) % copies], xs[B], B)
 
     stream = torch.cuda.Stream(device=dev)
+    if world > 1:  # fused exchanges wait on the device for at most 2 s
+        dist.barrier()
     # warm-up (also configures kernel attributes before any capture)
     with torch.cuda.stream(stream):
         for i in range(3):
@@ -833,6 +840,40 @@ def bench_moe(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_kind, 
     wd = [d0] + [d0.clone() for _ in range(copies - 1)]
     mx = MoeExchange(H, max(Ts), dev) if world > 1 else None
     res = {}
+    parity = None
+    if world > 1:
+        # every T once: the expert-parallel layer is identical on every rank
+        # and within the MoE tolerance of spiral_moe_ffn over all 128 experts
+        # on this rank (a different summation order, so not bitwise)
+        import torch.distributed as dist
+
+        ga, ua, da = (torch.from_numpy(a).to(dev) for a in (g_all, u_all, d_all))
+        worst, differ = 0.0, 0
+        for T in Ts:
+            x = torch.from_numpy(F.gen_activations(T, H, seed=T).view(np.int16)).to(dev).view(torch.bfloat16)
+            ids, wts = (torch.from_numpy(a).to(dev) for a in F.gen_routing(T, E, topk, seed=1000 * T))
+            dist.barrier()
+            y_ep = sp.moe_ffn_ep(fid, g0, u0, d0, x, ids, wts, hidden=H, inter=I, n_experts_local=El,
+                                 expert_first=e0, exchange_peers_dev=mx.peers, rank=rank, world=world,
+                                 max_tokens=mx.max_tokens, y_dtype=sp.F32)
+            y_1 = sp.moe_ffn(fid, ga, ua, da, x, ids, wts, hidden=H, inter=I, n_experts_local=E, y_dtype=sp.F32)
+            torch.cuda.synchronize()
+            ys = [torch.empty_like(y_ep) for _ in range(world)]
+            dist.all_gather(ys, y_ep)
+            differ += sum(int((a.view(torch.int32) != y_ep.view(torch.int32)).sum().item()) for a in ys)
+            rms = float(y_1.square().mean().sqrt())
+            worst = max(worst, float(((y_ep - y_1).abs() / (y_1.abs() + rms)).max()))
+        del ga, ua, da
+        st = sp.device_status()
+        t = torch.tensor([differ, st, worst], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        differ, st, worst = int(t[0]), int(t[1]), float(t[2])
+        ok = differ == 0 and st == 0 and worst <= 2e-3
+        parity = {"check": "identical on every rank; vs spiral_moe_ffn over all experts on one GPU, "
+                           "|d| <= 2e-3 (|y| + rms(y)), every T", "rank_mismatches": differ,
+                  "max_rel": worst, "device_status": st, "status": "ok" if ok else "FAIL"}
+        if not ok:
+            raise SystemExit(f"rank {rank}: expert-parallel MoE parity failed: {parity}")
     for T in Ts:
         x = torch.from_numpy(F.gen_activations(T, H, seed=T).view(np.int16)).to(dev).view(torch.bfloat16)
         rts = [F.gen_routing(T, E, topk, seed=1000 * T + r) for r in range(routings)]
@@ -870,6 +911,8 @@ def bench_moe(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_kind, 
     if mx is not None:
         torch.cuda.synchronize()
         del mx
+    if parity is not None:
+        res["parity"] = parity
     return res
 
 

@@ -70,6 +70,16 @@ __device__ __forceinline__ float byte_as_f32_magic(uint32_t w) {
   return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | I));
 }
 
+// ----------------------------------------- programmatic dependent launch --
+// A kernel launched with programmatic stream serialization lets its
+// successor be scheduled once every CTA has called launch_dependents, and
+// must call griddep_wait before it reads anything its predecessor wrote (the
+// wait returns when the predecessor has completed and its writes are visible).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // --------------------------------------------------------- shared memory --
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -35,56 +35,39 @@ template <> struct DequantUnit<kQ6_K> {
 
 constexpr int kDequantWarps = 8;
 
-// Row-major output, fast path.  Preconditions (checked on the host): src,
-// dst 16-byte aligned; src_stride and dst_stride*2 multiples of 16; K a
-// multiple of kGroupK.
-template <int FMT, bool FTZ>
-__global__ void __launch_bounds__(kDequantWarps * 32)
-    dequant_rows_fast(const uint8_t* __restrict__ src, int64_t src_stride, uint16_t* __restrict__ dst,
-                      int64_t dst_stride, int64_t groups_per_row, int64_t total_groups) {
+// Offsets of a unit's groups: one 32-bit division per unit (the host
+// guarantees total_groups < 2^32); the unit's later groups step along the row
+// and wrap to the next rows.
+template <int FMT>
+__device__ __forceinline__ void dq_unit_offsets(int64_t unit, int64_t groups_per_row, int64_t total_groups,
+                                                int64_t src_stride, int64_t dst_stride,
+                                                int64_t (&src_off)[DequantUnit<FMT>::kGroups],
+                                                int64_t (&dst_off)[DequantUnit<FMT>::kGroups],
+                                                bool (&valid)[DequantUnit<FMT>::kGroups]) {
   using U = DequantUnit<FMT>;
-  constexpr int kUnitBytes = U::kGroupBytes * U::kGroups;
-  constexpr int kLoads = kUnitBytes / 16;
-  // +16: lds_u32_a2 may read one word past the last used byte.
-  __shared__ __align__(16) uint8_t sbuf[kDequantWarps][kUnitBytes + 16];
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t unit = static_cast<int64_t>(blockIdx.x) * kDequantWarps + warp;
   const int64_t g0 = unit * U::kGroups;
-  if (g0 >= total_groups) return;
-  uint8_t* buf = sbuf[warp];
-
-  // One 32-bit division per unit (the host guarantees total_groups < 2^32);
-  // the unit's later groups step along the row and wrap to the next rows.
-  int64_t src_off[U::kGroups], dst_off[U::kGroups];
-  bool valid[U::kGroups];
-  {
-    const uint32_t gpr = static_cast<uint32_t>(groups_per_row);
-    uint32_t row = static_cast<uint32_t>(g0) / gpr;
-    uint32_t gi = static_cast<uint32_t>(g0) - row * gpr;
+  const uint32_t gpr = static_cast<uint32_t>(groups_per_row);
+  uint32_t row = static_cast<uint32_t>(g0) / gpr;
+  uint32_t gi = static_cast<uint32_t>(g0) - row * gpr;
 #pragma unroll
-    for (int g = 0; g < U::kGroups; ++g) {
-      valid[g] = g0 + g < total_groups;
-      src_off[g] = static_cast<int64_t>(row) * src_stride + static_cast<int64_t>(gi) * U::kGroupBytes;
-      dst_off[g] = static_cast<int64_t>(row) * dst_stride + static_cast<int64_t>(gi) * U::kGroupK;
-      if (++gi == gpr) {
-        gi = 0;
-        ++row;
-      }
+  for (int g = 0; g < U::kGroups; ++g) {
+    valid[g] = g0 + g < total_groups;
+    src_off[g] = static_cast<int64_t>(row) * src_stride + static_cast<int64_t>(gi) * U::kGroupBytes;
+    dst_off[g] = static_cast<int64_t>(row) * dst_stride + static_cast<int64_t>(gi) * U::kGroupK;
+    if (++gi == gpr) {
+      gi = 0;
+      ++row;
     }
   }
+}
 
-  constexpr int kPieces = U::kGroupBytes / 16;
-#pragma unroll
-  for (int q = lane; q < kLoads; q += 32) {
-    const int g = q / kPieces, piece = q - g * kPieces;
-    if (valid[g]) {
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + src_off[g] + 16 * piece));
-      *reinterpret_cast<uint4*>(buf + 16 * q) = v;
-    }
-  }
-  __syncwarp();
-
+// Decode one unit staged in shared memory and store it: lanes write
+// consecutive 16-byte chunks, so each store instruction covers a contiguous
+// 512-byte run.
+template <int FMT, bool FTZ>
+__device__ __forceinline__ void dq_unit_store(const uint8_t* buf, int lane, uint16_t* __restrict__ dst,
+                                              const int64_t (&dst_off)[DequantUnit<FMT>::kGroups],
+                                              const bool (&valid)[DequantUnit<FMT>::kGroups]) {
   if constexpr (FMT == kQ4_0 || FMT == kQ8_0) {
     constexpr int kBB = Fmt<FMT>::kBlockBytes;
 #pragma unroll
@@ -127,6 +110,125 @@ __global__ void __launch_bounds__(kDequantWarps * 32)
       }
     }
   }
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Row-major output, fast path.  Preconditions (checked on the host): src,
+// dst 16-byte aligned; src_stride and dst_stride*2 multiples of 16; K a
+// multiple of kGroupK.  A resident grid: every warp walks the units
+// gw, gw + nw, ... and keeps kDqDepth of them in flight in a private ring of
+// shared buffers (16-byte cp.async per lane), so the reads of the next units
+// overlap the decode and the stores of this one.
+constexpr int kDqDepth = 3;
+template <int FMT, bool FTZ>
+__global__ void __launch_bounds__(kDequantWarps * 32)
+    dequant_rows_pipe(const uint8_t* __restrict__ src, int64_t src_stride, uint16_t* __restrict__ dst,
+                      int64_t dst_stride, int64_t groups_per_row, int64_t total_groups, int64_t units) {
+  using U = DequantUnit<FMT>;
+  constexpr int kUnitBytes = U::kGroupBytes * U::kGroups;
+  constexpr int kLoads = kUnitBytes / 16;
+  constexpr int kPieces = U::kGroupBytes / 16;
+  // +16: lds_u32_a2 may read one word past the last used byte.
+  constexpr int kSlot = kUnitBytes + 16;
+  __shared__ __align__(16) uint8_t sbuf[kDequantWarps][kDqDepth][kSlot];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kDequantWarps + warp;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * kDequantWarps;
+  // programmatic dependent launch: the next kernel may be scheduled now; this
+  // one touches global memory only after its predecessor has completed
+  griddep_launch_dependents();
+  griddep_wait();
+
+  // one commit group per unit slot, empty past the last unit
+  auto issue = [&](int64_t u, int slot) {
+    if (u < units) {
+      int64_t so[U::kGroups], dof[U::kGroups];
+      bool v[U::kGroups];
+      dq_unit_offsets<FMT>(u, groups_per_row, total_groups, src_stride, 0, so, dof, v);
+      uint8_t* buf = sbuf[warp][slot];
+#pragma unroll
+      for (int q = lane; q < kLoads; q += 32) {
+        const int g = q / kPieces, piece = q - g * kPieces;
+        // select the group's offset without indexing the arrays by a
+        // run-time value (which would put them in local memory)
+        int64_t off = so[0];
+        bool ok = v[0];
+#pragma unroll
+        for (int gg = 1; gg < U::kGroups; ++gg) {
+          if (g == gg) {
+            off = so[gg];
+            ok = v[gg];
+          }
+        }
+        if (ok) cp_async16(buf + 16 * q, src + off + 16 * piece);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int s = 0; s < kDqDepth; ++s) issue(gw + s * nw, s);
+
+  int slot = 0;
+  for (int64_t u = gw; u < units; u += nw) {
+    cp_async_wait<kDqDepth - 1>();  // this lane's pieces of unit u have landed ...
+    __syncwarp();                   // ... and every other lane's
+    int64_t so[U::kGroups], dof[U::kGroups];
+    bool v[U::kGroups];
+    dq_unit_offsets<FMT>(u, groups_per_row, total_groups, 0, dst_stride, so, dof, v);
+    dq_unit_store<FMT, FTZ>(sbuf[warp][slot], lane, dst, dof, v);
+    __syncwarp();  // the slot is read by every lane before it is refilled
+    issue(u + kDqDepth * nw, slot);
+    slot = slot + 1 == kDqDepth ? 0 : slot + 1;
+  }
+  cp_async_wait<0>();
+}
+
+// Row-major output, fast path, one unit per warp (no ring): the better
+// choice for Q6_K, whose units are large (2048 weights) and whose decode
+// needs more registers than a resident ring of units allows.
+template <int FMT, bool FTZ>
+__global__ void __launch_bounds__(kDequantWarps * 32)
+    dequant_rows_unit(const uint8_t* __restrict__ src, int64_t src_stride, uint16_t* __restrict__ dst,
+                      int64_t dst_stride, int64_t groups_per_row, int64_t total_groups, int64_t units) {
+  using U = DequantUnit<FMT>;
+  constexpr int kUnitBytes = U::kGroupBytes * U::kGroups;
+  constexpr int kLoads = kUnitBytes / 16;
+  constexpr int kPieces = U::kGroupBytes / 16;
+  __shared__ __align__(16) uint8_t sbuf[kDequantWarps][kUnitBytes + 16];
+  griddep_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t unit = static_cast<int64_t>(blockIdx.x) * kDequantWarps + warp;
+  if (unit >= units) return;
+  int64_t so[U::kGroups], dof[U::kGroups];
+  bool v[U::kGroups];
+  dq_unit_offsets<FMT>(unit, groups_per_row, total_groups, src_stride, dst_stride, so, dof, v);
+  griddep_wait();
+  uint8_t* buf = sbuf[warp];
+#pragma unroll
+  for (int q = lane; q < kLoads; q += 32) {
+    const int g = q / kPieces, piece = q - g * kPieces;
+    int64_t off = so[0];
+    bool ok = v[0];
+#pragma unroll
+    for (int gg = 1; gg < U::kGroups; ++gg) {
+      if (g == gg) {
+        off = so[gg];
+        ok = v[gg];
+      }
+    }
+    if (ok) *reinterpret_cast<uint4*>(buf + 16 * q) = __ldg(reinterpret_cast<const uint4*>(src + off + 16 * piece));
+  }
+  __syncwarp();
+  dq_unit_store<FMT, FTZ>(buf, lane, dst, dof, v);
 }
 
 // Row-major output, any valid shape/alignment: one thread per 8-weight
@@ -201,9 +303,29 @@ static cudaError_t launch_rows(const uint8_t* src, int64_t src_stride, uint16_t*
     const int64_t gpr = K / U::kGroupK;
     const int64_t total_groups = gpr * N;
     const int64_t units = (total_groups + U::kGroups - 1) / U::kGroups;
-    const int64_t blocks = (units + kDequantWarps - 1) / kDequantWarps;
-    dequant_rows_fast<FMT, FTZ><<<static_cast<unsigned>(blocks), kDequantWarps * 32, 0, stream>>>(
-        src, src_stride, dst, dst_stride, gpr, total_groups);
+    int64_t blocks = (units + kDequantWarps - 1) / kDequantWarps;
+    auto* kernel = FMT == kQ6_K ? dequant_rows_unit<FMT, FTZ> : dequant_rows_pipe<FMT, FTZ>;
+    if (FMT != kQ6_K) {
+      static int per_sm[2] = {0, 0};  // resident CTAs per SM (same on every B200)
+      const int slot = FMT == kQ4_0 ? 0 : 1;
+      if (per_sm[slot] == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kDequantWarps * 32, 0) != cudaSuccess || n < 1)
+          n = 1;
+        per_sm[slot] = n;
+      }
+      blocks = std::min<int64_t>(blocks, int64_t(device_sm_count()) * per_sm[slot]);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+    cfg.blockDim = dim3(kDequantWarps * 32);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, src, src_stride, dst, dst_stride, gpr, total_groups, units);
   } else {
     const int64_t total = (K / 8) * N;
     const int64_t blocks = std::min<int64_t>((total + 255) / 256, int64_t(148) * 64);
