@@ -51,8 +51,20 @@ extern "C" {
 typedef enum spiral_qfmt {
   SPIRAL_QFMT_Q4_0 = 2,  /* 18-byte block: fp16 d, 16 B nibbles; w=(q-8)*d   */
   SPIRAL_QFMT_Q8_0 = 8,  /* 34-byte block: fp16 d, 32 int8;      w=q*d       */
-  SPIRAL_QFMT_Q6_K = 14  /* 210-byte super-block of 256: ql[128] qh[64]
+  SPIRAL_QFMT_Q6_K = 14, /* 210-byte super-block of 256: ql[128] qh[64]
                             sc[16] d; w=d*sc*(q-32)                          */
+  /* Extended formats (ggml's layouts; spiral_dequant_bf16, spiral_mul_mat
+   * and the ggml boundary only, K a multiple of the block size and of 8):  */
+  SPIRAL_QFMT_F16 = 1,     /* 2 bytes per weight; w = bf16_rne(f16)          */
+  SPIRAL_QFMT_Q4_K = 12,   /* 144-byte super-block of 256: fp16 d, dmin,
+                              12 B of 6-bit (scale, min) pairs, 128 B nibbles;
+                              w = (d*sc)*q - dmin*m                          */
+  SPIRAL_QFMT_Q5_K = 13,   /* 176 bytes: Q4_K plus qh[32] (the fifth bit)    */
+  SPIRAL_QFMT_IQ4_NL = 20, /* 18-byte block of 32: fp16 d, 16 B codebook
+                              nibbles; w = d * kvalues[q]                    */
+  SPIRAL_QFMT_IQ4_XS = 23, /* 136-byte super-block of 256: fp16 d, 6-bit
+                              sub-scales ls; w = (d*(ls-32)) * kvalues[q]    */
+  SPIRAL_QFMT_BF16 = 30    /* 2 bytes per weight, used as is                 */
 } spiral_qfmt;
 
 /* Output element types (ggml type ids). */
@@ -109,7 +121,9 @@ SPIRAL_API int spiral_device_status(void* stream, uint32_t* code);
 /* Weights per block (32, 32, 256) and bytes per block (18, 34, 210); 0 for an
  * unknown format.  Mirrors the per-format kBlockRows / kBlockBytes constants
  * of src/quants/<fmt>/layout.h (q4_0/layout.h:10-12, q8_0/layout.h:10-13,
- * q6_k/layout.h:10-15). */
+ * q6_k/layout.h:10-15).  The extended formats report ggml's block and type
+ * sizes (Q4_K 256/144, Q5_K 256/176, IQ4_NL 32/18, IQ4_XS 256/136, F16 and
+ * BF16 1/2). */
 SPIRAL_API int64_t spiral_quants_block_rows(int fmt);
 SPIRAL_API int64_t spiral_quants_block_bytes(int fmt);
 

@@ -20,13 +20,16 @@ PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libspiral_b200.so"
 
 Q4_0, Q8_0, Q6_K = 2, 8, 14
+# extended formats (spiral_dequant_bf16 / spiral_mul_mat / the ggml boundary)
+F16, Q4_K, Q5_K, IQ4_NL, IQ4_XS = 1, 12, 13, 20, 23
 F32, BF16 = 0, 30
 FLAG_FTZ_SCALES = 0x1
 FLAG_ACCUMULATE = 0x2
 FLAG_STATIC_WEIGHTS = 0x4
-FORMATS = {"q4_0": Q4_0, "q8_0": Q8_0, "q6_k": Q6_K}
-BLOCK_K = {Q4_0: 32, Q8_0: 32, Q6_K: 256}
-BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q6_K: 210}
+FORMATS = {"q4_0": Q4_0, "q8_0": Q8_0, "q6_k": Q6_K, "q4_k": Q4_K, "q5_k": Q5_K, "iq4_nl": IQ4_NL,
+           "iq4_xs": IQ4_XS, "f16": F16, "bf16": BF16}
+BLOCK_K = {Q4_0: 32, Q8_0: 32, Q6_K: 256, Q4_K: 256, Q5_K: 256, IQ4_NL: 32, IQ4_XS: 256, F16: 1, BF16: 1}
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q6_K: 210, Q4_K: 144, Q5_K: 176, IQ4_NL: 18, IQ4_XS: 136, F16: 2, BF16: 2}
 
 # Every symbol include/spiral_b200.h declares, with (argtypes, restype).
 _i64, _i32, _vp, _u32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_uint

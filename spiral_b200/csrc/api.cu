@@ -6,6 +6,7 @@
 // fails with SPIRAL_ERR_CUDA and a message from spiral_last_error().
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -35,13 +36,23 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(SPIRAL_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
+// The reference's three formats (every entry point) ...
 bool fmt_valid(int fmt) { return fmt == kQ4_0 || fmt == kQ8_0 || fmt == kQ6_K; }
+// ... and the extended ones (dequant and MUL_MAT only).
+bool fmt_valid_any(int fmt) { return fmt_valid(fmt) || fmt_is_ext(fmt); }
 
+// ggml's block size (weights) and type size (bytes) of each format.
 int64_t block_k(int fmt) {
   switch (fmt) {
     case kQ4_0: return 32;
     case kQ8_0: return 32;
     case kQ6_K: return 256;
+    case kQ4_K: return 256;
+    case kQ5_K: return 256;
+    case kIQ4_NL: return 32;
+    case kIQ4_XS: return 256;
+    case kF16: return 1;
+    case kBF16: return 1;
   }
   return 0;
 }
@@ -50,6 +61,12 @@ int64_t block_bytes(int fmt) {
     case kQ4_0: return 18;
     case kQ8_0: return 34;
     case kQ6_K: return 210;
+    case kQ4_K: return 144;
+    case kQ5_K: return 176;
+    case kIQ4_NL: return 18;
+    case kIQ4_XS: return 136;
+    case kF16: return 2;
+    case kBF16: return 2;
   }
   return 0;
 }
@@ -66,13 +83,20 @@ int current_device() {
   return dev;
 }
 
-int check_shape(int fmt, int64_t K, int64_t N) {
-  if (!fmt_valid(fmt)) return fail(SPIRAL_ERR_INVALID_FORMAT, "unknown quantized format %d", fmt);
+// any_fmt: the entry point also takes the extended formats (whose kernels
+// work in 8-weight chunks, so K must be a multiple of 8 for F16/BF16 too).
+int check_shape(int fmt, int64_t K, int64_t N, bool any_fmt = false) {
+  if (!(any_fmt ? fmt_valid_any(fmt) : fmt_valid(fmt))) {
+    if (fmt_valid_any(fmt))
+      return fail(SPIRAL_ERR_UNSUPPORTED, "format %d is supported by dequant and MUL_MAT only", fmt);
+    return fail(SPIRAL_ERR_INVALID_FORMAT, "unknown quantized format %d", fmt);
+  }
   if (K <= 0 || N <= 0) return fail(SPIRAL_ERR_INVALID_SHAPE, "dims must be positive (K=%lld N=%lld)", (long long)K,
                                     (long long)N);
-  if (K % block_k(fmt) != 0)
+  const int64_t unit = std::max<int64_t>(block_k(fmt), 8);
+  if (K % unit != 0)
     return fail(SPIRAL_ERR_INVALID_SHAPE, "K=%lld is not a multiple of the block size %lld", (long long)K,
-                (long long)block_k(fmt));
+                (long long)unit);
   return SPIRAL_OK;
 }
 
@@ -126,8 +150,8 @@ const char* spiral_status_string(int status) {
 
 const char* spiral_last_error(void) { return g_last_error; }
 
-int64_t spiral_quants_block_rows(int fmt) { return fmt_valid(fmt) ? block_k(fmt) : 0; }
-int64_t spiral_quants_block_bytes(int fmt) { return fmt_valid(fmt) ? block_bytes(fmt) : 0; }
+int64_t spiral_quants_block_rows(int fmt) { return fmt_valid_any(fmt) ? block_k(fmt) : 0; }
+int64_t spiral_quants_block_bytes(int fmt) { return fmt_valid_any(fmt) ? block_bytes(fmt) : 0; }
 
 int64_t spiral_quants_record_count(int fmt, int64_t weights_rows, int64_t weights_cols) {
   if (!fmt_valid(fmt) || weights_rows <= 0 || weights_cols <= 0 || weights_rows % block_k(fmt) != 0) return 0;
@@ -162,7 +186,7 @@ void spiral_set_repack_warn(spiral_repack_warn_fn_t fn, void* user) { repack_set
 int spiral_dequant_bf16(int fmt, const void* src, int64_t src_row_stride_bytes, void* dst,
                         int64_t dst_row_stride_elems, int64_t K, int64_t N, unsigned flags, void* stream) {
   g_last_error[0] = 0;
-  if (int st = check_shape(fmt, K, N)) return st;
+  if (int st = check_shape(fmt, K, N, true)) return st;
   if (src == nullptr || dst == nullptr) return fail(SPIRAL_ERR_NULL_POINTER, "null src or dst");
   if (src_row_stride_bytes < row_bytes(fmt, K))
     return fail(SPIRAL_ERR_INVALID_SHAPE, "src row stride %lld < row bytes %lld", (long long)src_row_stride_bytes,
@@ -230,7 +254,7 @@ int spiral_mul_mat(int fmt, const void* w, int64_t w_row_stride_bytes, const voi
                    void* y, int y_dtype, int64_t y_row_stride_elems, int64_t M, int64_t N, int64_t K, unsigned flags,
                    void* stream) {
   g_last_error[0] = 0;
-  if (int st = check_shape(fmt, K, N)) return st;
+  if (int st = check_shape(fmt, K, N, true)) return st;
   if (M <= 0) return fail(SPIRAL_ERR_INVALID_SHAPE, "M=%lld must be positive", (long long)M);
   if (w == nullptr || x == nullptr || y == nullptr) return fail(SPIRAL_ERR_NULL_POINTER, "null w, x or y");
   if (y_dtype != SPIRAL_DTYPE_BF16 && y_dtype != SPIRAL_DTYPE_F32)

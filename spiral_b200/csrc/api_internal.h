@@ -39,6 +39,12 @@ struct MatArgs {
   int64_t M, N, K;
 };
 
+// formats_ext.cu — Q4_K, Q5_K, IQ4_NL, IQ4_XS, F16, BF16.
+bool fmt_is_ext(int fmt);
+cudaError_t dequant_rows_ext(int fmt, const void* src, int64_t src_stride, void* dst, int64_t dst_stride, int64_t K,
+                             int64_t N, bool ftz, cudaStream_t stream);
+cudaError_t gemv_ext(const MatArgs& a, cudaStream_t stream);
+
 // gemv.cu — M <= 8.
 bool gemv_fast_ok(const MatArgs& a);
 cudaError_t gemv(const MatArgs& a, cudaStream_t stream);

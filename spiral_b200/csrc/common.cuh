@@ -22,11 +22,21 @@
 namespace spiral {
 
 enum : int { kQ4_0 = 2, kQ8_0 = 8, kQ6_K = 14 };
+// Extended formats (ggml type ids): the K-quants Q4_K / Q5_K, the codebook
+// formats IQ4_NL / IQ4_XS and the 2-byte pass-through types.
+enum : int { kF16 = 1, kQ4_K = 12, kQ5_K = 13, kIQ4_NL = 20, kIQ4_XS = 23, kBF16 = 30 };
 
 template <int FMT> struct Fmt;
 template <> struct Fmt<kQ4_0> { static constexpr int kBlockK = 32;  static constexpr int kBlockBytes = 18; };
 template <> struct Fmt<kQ8_0> { static constexpr int kBlockK = 32;  static constexpr int kBlockBytes = 34; };
 template <> struct Fmt<kQ6_K> { static constexpr int kBlockK = 256; static constexpr int kBlockBytes = 210; };
+template <> struct Fmt<kQ4_K> { static constexpr int kBlockK = 256; static constexpr int kBlockBytes = 144; };
+template <> struct Fmt<kQ5_K> { static constexpr int kBlockK = 256; static constexpr int kBlockBytes = 176; };
+template <> struct Fmt<kIQ4_NL> { static constexpr int kBlockK = 32; static constexpr int kBlockBytes = 18; };
+template <> struct Fmt<kIQ4_XS> { static constexpr int kBlockK = 256; static constexpr int kBlockBytes = 136; };
+// The 2-byte types are handled in chunks of 8 values (16 bytes).
+template <> struct Fmt<kF16> { static constexpr int kBlockK = 8; static constexpr int kBlockBytes = 16; };
+template <> struct Fmt<kBF16> { static constexpr int kBlockK = 8; static constexpr int kBlockBytes = 16; };
 
 // Device-wide sticky error word.  Bounded waits that give up OR a code in here
 // instead of trapping; the host reads and clears it (spiral_device_status).

@@ -369,6 +369,7 @@ cudaError_t dequant_rows(int fmt, const void* src, int64_t src_stride, void* dst
     case kQ6_K: SPIRAL_DQ(kQ6_K);
   }
 #undef SPIRAL_DQ
+  if (fmt_is_ext(fmt)) return dequant_rows_ext(fmt, src, src_stride, dst, dst_stride, K, N, ftz, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -12,20 +12,22 @@
 
 namespace {
 
-int64_t ggml_block_k(int t) { return t == SPIRAL_QFMT_Q6_K ? 256 : 32; }
-int64_t ggml_block_bytes(int t) { return t == SPIRAL_QFMT_Q4_0 ? 18 : (t == SPIRAL_QFMT_Q8_0 ? 34 : 210); }
+// ggml's block size / type size; 0 for a type spiral_mul_mat does not take
+// (every quantized format of spiral_qfmt and the F16 / BF16 pass-through).
+int64_t ggml_block_k(int t) { return spiral_quants_block_rows(t); }
+int64_t ggml_block_bytes(int t) { return spiral_quants_block_bytes(t); }
 
 // 0 when the node is served, else the spiral_status that refuses it.
 int ggml_check(const spiral_ggml_tensor* a, const spiral_ggml_tensor* b, const spiral_ggml_tensor* d) {
   if (a == nullptr || b == nullptr || d == nullptr) return SPIRAL_ERR_NULL_POINTER;
-  if (a->type != SPIRAL_QFMT_Q4_0 && a->type != SPIRAL_QFMT_Q8_0 && a->type != SPIRAL_QFMT_Q6_K)
-    return SPIRAL_ERR_INVALID_FORMAT;
+  if (ggml_block_k(a->type) <= 0) return SPIRAL_ERR_INVALID_FORMAT;
   if (b->type != SPIRAL_DTYPE_BF16) return SPIRAL_ERR_UNSUPPORTED;
   if (d->type != SPIRAL_DTYPE_BF16 && d->type != SPIRAL_DTYPE_F32) return SPIRAL_ERR_UNSUPPORTED;
   for (int i = 0; i < 4; ++i)
     if (a->ne[i] <= 0 || b->ne[i] <= 0 || d->ne[i] <= 0) return SPIRAL_ERR_INVALID_SHAPE;
   const int64_t K = a->ne[0];
-  if (b->ne[0] != K || K % ggml_block_k(a->type) != 0) return SPIRAL_ERR_INVALID_SHAPE;
+  // whole blocks, and whole 8-weight chunks for the 2-byte types
+  if (b->ne[0] != K || K % ggml_block_k(a->type) != 0 || K % 8 != 0) return SPIRAL_ERR_INVALID_SHAPE;
   if (d->ne[0] != a->ne[1] || d->ne[1] != b->ne[1] || d->ne[2] != b->ne[2] || d->ne[3] != b->ne[3])
     return SPIRAL_ERR_INVALID_SHAPE;
   if (b->ne[2] % a->ne[2] != 0 || b->ne[3] % a->ne[3] != 0) return SPIRAL_ERR_INVALID_SHAPE;

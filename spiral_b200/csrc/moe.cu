@@ -15,12 +15,13 @@
 // serialization (every kernel waits for its predecessor before it reads
 // anything that predecessor wrote):
 //   1. moe_route   one CTA: bucket the (token, slot) pairs of local experts by
-//                  expert (counting sort) and cut each expert's pairs into
-//                  problems of at most 8 (the MMA N width).
+//                  expert (a parallel counting sort) and cut each expert's
+//                  pairs into problems of at most 8 (the MMA N width).
 //   2. moe_gemv<1> gate+up: work item = (problem, 16 intermediate features);
 //                  a stage holds the 16 gate rows and the 16 up rows; the
 //                  epilogue applies SwiGLU and stores h in bf16.
-//   3. moe_gemv<2> down: work item = (problem, 16 output features); the
+//   3. moe_gemv<2> down: work item = (problem, 64 output features: four MMA
+//                  row blocks, each split over two warps by K); the
 //                  epilogue stores w_{t,j} * y_e in fp32 per pair.
 //   4. moe_combine y_t = sum over slots j in order (deterministic).
 // The grouped GEMVs reuse the decode GEMV's machinery (gemv_decode.cuh): one
@@ -111,11 +112,44 @@ struct MoeArgs {
 
 // ------------------------------------------------------------- routing ----
 
+// Exclusive prefix sum of v over the block (kRouteThreads threads, one value
+// each); returns this thread's prefix and sets `total`.
+__device__ __forceinline__ int route_scan(int v, int* warp_sums, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < kRouteThreads / 32 ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    warp_sums[lane] = w;  // inclusive
+  }
+  __syncthreads();
+  const int before = (warp > 0 ? warp_sums[warp - 1] : 0) + x - v;
+  total = warp_sums[kRouteThreads / 32 - 1];
+  __syncthreads();  // warp_sums is reused by the next scan
+  return before;
+}
+
+// Counting sort of the local (token, slot) pairs by expert, every step in
+// parallel: counts by shared atomics, one block scan for each expert's first
+// pair and one for its first problem, then each expert writes its own
+// problems.  E_local is processed in chunks of kRouteThreads experts.
 __global__ void __launch_bounds__(kRouteThreads) moe_route(const MoeArgs a) {
   extern __shared__ int sh[];
   int* scnt = sh;
   int* sstart = sh + a.E_local;
   int* scur = sh + 2 * a.E_local;
+  __shared__ int warp_sums[32];
   griddep_launch_dependents();
   griddep_wait();
   int* hdr = reinterpret_cast<int*>(a.ws + a.L.hdr);
@@ -132,20 +166,28 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route(const MoeArgs a) {
     if (e >= 0 && e < a.E_local) atomicAdd(&scnt[e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0, np = 0;
-    for (int e = 0; e < a.E_local; ++e) {
-      sstart[e] = run;
-      for (int c = 0; c < scnt[e]; c += 8) {
+  int run = 0, np = 0;  // pairs and problems before this chunk
+  for (int e0 = 0; e0 < a.E_local; e0 += kRouteThreads) {
+    const int e = e0 + static_cast<int>(threadIdx.x);
+    const int cnt = e < a.E_local ? scnt[e] : 0;
+    int pairs_chunk = 0, probs_chunk = 0;
+    const int pbefore = route_scan(cnt, warp_sums, pairs_chunk);
+    const int qbefore = route_scan((cnt + 7) / 8, warp_sums, probs_chunk);
+    if (e < a.E_local) {
+      sstart[e] = run + pbefore;
+      for (int c = 0, q = np + qbefore; c < cnt; c += 8, ++q) {
         MoeProblem pr;
         pr.expert = e;
-        pr.first = run + c;
-        pr.nx = min(8, scnt[e] - c);
+        pr.first = run + pbefore + c;
+        pr.nx = min(8, cnt - c);
         pr.pad = 0;
-        probs[np++] = pr;
+        probs[q] = pr;
       }
-      run += scnt[e];
     }
+    run += pairs_chunk;
+    np += probs_chunk;
+  }
+  if (threadIdx.x == 0) {
     hdr[0] = np;
     hdr[1] = run;
   }
@@ -167,9 +209,13 @@ struct MoePhase<1> {  // gate + up, K = H, 16 intermediate features per item
   static constexpr int kRows = 32;
 };
 template <>
-struct MoePhase<2> {  // down, K = I, 16 output features per item
-  static constexpr int kRows = 16;
+struct MoePhase<2> {  // down, K = I, up to 64 output features per item
+  static constexpr int kRows = 64;
 };
+// Output features per work item: 16 for gate/up (the stage holds those 16
+// gate rows and 16 up rows); for down 64, 32 or 16 (the most that leaves
+// three stages in shared memory): 1, 2 or 4 MMA row blocks, each split by K
+// over 8, 4 or 2 warps, so every consumer warp decodes several groups.
 
 // Stage the activation rows of one problem for one consumer group in the
 // permuted fragment order of gemv_decode.cuh: row m (< nx) comes from
@@ -232,14 +278,17 @@ __device__ __forceinline__ void moe_decode_group(const uint8_t* ra, const uint8_
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
 template <int FMT, int PHASE>
-__global__ void __launch_bounds__(kMoeThreads, 1) moe_gemv(const MoeArgs a, int stages, int row_pitch, int x_pitch) {
+__global__ void __launch_bounds__(kMoeThreads, 1)
+    moe_gemv(const MoeArgs a, int stages, int row_pitch, int x_pitch, int item_rows) {
   using F = GemvFmt<FMT>;
   using P = MoePhase<PHASE>;
   constexpr int kAcc = PHASE == 1 ? 2 : 1;
   const int K = PHASE == 1 ? a.H : a.I;
   const int N = PHASE == 1 ? a.I : a.H;
   const int64_t rb = PHASE == 1 ? a.rb_h : a.rb_i;
-  const int tiles = N / kTileRows;
+  const int kItemRows = PHASE == 1 ? kTileRows : item_rows;
+  const int stage_rows = PHASE == 1 ? P::kRows : item_rows;
+  const int tiles = N / kItemRows;
   const int groups_per_row = K / F::kGroupK;
 
   extern __shared__ __align__(128) uint8_t smem[];
@@ -249,7 +298,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_gemv(const MoeArgs a, int 
   float4* red = reinterpret_cast<float4*>(smem + kMoeBarrierBytes);  // [groups][kAcc][8 warps][32]
   uint8_t* xbuf = smem + kMoeBarrierBytes + kMoeConsumers * 32 * 16 * kAcc;  // [groups][8][x_pitch]
   uint8_t* stg = xbuf + kMoeGroups * 8 * x_pitch;
-  const int stage_bytes = P::kRows * row_pitch;
+  const int stage_bytes = stage_rows * row_pitch;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -287,20 +336,20 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_gemv(const MoeArgs a, int 
       if (lane == 0) {
         go = mbar_wait(&empty[s], ((it / stages) & 1u) ^ 1u) && !*(volatile int*)&abort_flag;
         if (go) {
-          mbar_arrive_expect_tx(&full[s], bytes * P::kRows);
+          mbar_arrive_expect_tx(&full[s], bytes * stage_rows);
         } else {
           abort_flag = 1;
         }
       }
       if (!__shfl_sync(0xffffffffu, go, 0)) break;
-      if (lane < P::kRows) {
-        uint8_t* dst = stg + s * stage_bytes + lane * row_pitch;
-        const int64_t row0 = static_cast<int64_t>(pr.expert) * N + tile * kTileRows;
+      const int64_t row0 = static_cast<int64_t>(pr.expert) * N + tile * kItemRows;
+      for (int l = lane; l < stage_rows; l += 32) {
+        uint8_t* dst = stg + s * stage_bytes + l * row_pitch;
         const uint8_t* src;
         if constexpr (PHASE == 1) {
-          src = lane < kTileRows ? a.w_gate + (row0 + lane) * rb : a.w_up + (row0 + lane - kTileRows) * rb;
+          src = l < kTileRows ? a.w_gate + (row0 + l) * rb : a.w_up + (row0 + l - kTileRows) * rb;
         } else {
-          src = a.w_down + (row0 + lane) * rb;
+          src = a.w_down + (row0 + l) * rb;
         }
         bulk_g2s(dst, src, bytes, &full[s], pol);
       }
@@ -350,12 +399,25 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_gemv(const MoeArgs a, int 
     }
     if (ready) {
       const uint8_t* st = stg + s * stage_bytes;
-      for (int gl = gw; gl < groups_per_row; gl += kMoeWarpsPerGroup) {
-        const uint8_t* xg = xcol + gl * (F::kSteps * 32);
+      if constexpr (PHASE == 1) {
+        for (int gl = gw; gl < groups_per_row; gl += kMoeWarpsPerGroup) {
+          const uint8_t* xg = xcol + gl * (F::kSteps * 32);
 #pragma unroll
-        for (int ac = 0; ac < kAcc; ++ac) {
-          const uint8_t* base = st + ac * kTileRows * row_pitch + gl * F::kGroupBytes;
-          moe_decode_group<FMT>(base + r * row_pitch, base + (r + 8) * row_pitch, c, xg, ftz, acc[ac], gl);
+          for (int ac = 0; ac < kAcc; ++ac) {
+            const uint8_t* base = st + ac * kTileRows * row_pitch + gl * F::kGroupBytes;
+            moe_decode_group<FMT>(base + r * row_pitch, base + (r + 8) * row_pitch, c, xg, ftz, acc[ac], gl);
+          }
+        }
+      } else {
+        // warp gw: row block gw / wpr of the item, the (gw % wpr)-th part of K
+        const int wpr = kMoeWarpsPerGroup / (item_rows / kTileRows);
+        const int per = (groups_per_row + wpr - 1) / wpr;
+        const int g_lo = (gw % wpr) * per, g_hi = min(groups_per_row, g_lo + per);
+        const uint8_t* base = st + (gw / wpr) * kTileRows * row_pitch;
+        for (int gl = g_lo; gl < g_hi; ++gl) {
+          const uint8_t* xg = xcol + gl * (F::kSteps * 32);
+          const uint8_t* gb = base + gl * F::kGroupBytes;
+          moe_decode_group<FMT>(gb + r * row_pitch, gb + (r + 8) * row_pitch, c, xg, ftz, acc[0], gl);
         }
       }
     }
@@ -365,7 +427,22 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_gemv(const MoeArgs a, int 
     for (int ac = 0; ac < kAcc; ++ac)
       gred[(ac * kMoeWarpsPerGroup + gw) * 32 + lane] = make_float4(acc[ac][0], acc[ac][1], acc[ac][2], acc[ac][3]);
     named_bar_sync(bar_id, kMoeGroupThreads);
-    if (gw < 4) {
+    if constexpr (PHASE == 2) {
+      // row blocks x 128 outputs: the K parts summed in order
+      const int wpr = kMoeWarpsPerGroup / (item_rows / kTileRows);
+      for (int idx = gt; idx < (item_rows / kTileRows) * 128; idx += kMoeGroupThreads) {
+        const int rbk = idx >> 7, l = (idx >> 2) & 31, j = idx & 3;
+        float v = 0.f;
+        for (int q = 0; q < wpr; ++q) v += reinterpret_cast<const float*>(&gred[(rbk * wpr + q) * 32 + l])[j];
+        const int row = rbk * kTileRows + (l >> 2) + 8 * (j >> 1);
+        const int m = 2 * (l & 3) + (j & 1);
+        if (ready && m < pr.nx) {
+          const int pair = pairs[pr.first + m];
+          float* part = reinterpret_cast<float*>(a.ws + a.L.part);
+          part[static_cast<int64_t>(pair) * a.H + tile * kItemRows + row] = a.wts[pair] * v;
+        }
+      }
+    } else if (gw < 4) {
       const int l = gt >> 2, j = gt & 3;
       float v[kAcc];
 #pragma unroll
@@ -575,11 +652,17 @@ cudaError_t launch_moe_gemv(const MoeArgs& a, cudaStream_t stream) {
   constexpr int kAcc = PHASE == 1 ? 2 : 1;
   const int K = PHASE == 1 ? a.H : a.I;
   const int64_t rb = PHASE == 1 ? a.rb_h : a.rb_i;
-  const int rows = MoePhase<PHASE>::kRows;
   const int x_pitch = K * 2 + 32;
   const int row_pitch = static_cast<int>(rb) + 16;
   const size_t fixed = kMoeBarrierBytes + size_t(kMoeConsumers) * 32 * 16 * kAcc + size_t(kMoeGroups) * 8 * x_pitch;
   const size_t avail = device_max_smem_optin();
+  // gate/up: 32 stage rows (16 gate + 16 up); down: the largest item of
+  // 64 / 32 / 16 rows that leaves three stages (the output dimension H is a
+  // multiple of 64)
+  int rows = MoePhase<PHASE>::kRows;
+  if constexpr (PHASE == 2) {
+    while (rows > kTileRows && fixed + size_t(3) * rows * row_pitch > avail) rows /= 2;
+  }
   if (fixed + size_t(2) * rows * row_pitch > avail) return cudaErrorInvalidValue;
   const int stages = static_cast<int>(std::min<size_t>(kMoeMaxStages, (avail - fixed) / (size_t(rows) * row_pitch)));
   const size_t smem = fixed + size_t(stages) * rows * row_pitch;
@@ -594,8 +677,8 @@ cudaError_t launch_moe_gemv(const MoeArgs& a, cudaStream_t stream) {
     configured[dev & 63].store(true, std::memory_order_release);
   }
   MoeArgs args = a;
-  int st = stages, rp = row_pitch, xp = x_pitch;
-  void* kargs[] = {&args, &st, &rp, &xp};
+  int st = stages, rp = row_pitch, xp = x_pitch, ir = rows;
+  void* kargs[] = {&args, &st, &rp, &xp, &ir};
   return launch_pdl(reinterpret_cast<const void*>(moe_gemv<FMT, PHASE>), dim3(device_sm_count()), dim3(kMoeThreads),
                     smem, stream, kargs);
 }

@@ -247,7 +247,7 @@ def test_ggml_supports_mul_mat_follows_ggml_rules():
         return src0, src1, dst
 
     assert sp.ggml_supports_mul_mat(*node())
-    for t0 in (sp.Q8_0, sp.Q6_K):
+    for t0 in (sp.Q8_0, sp.Q6_K, sp.Q4_K, sp.Q5_K, sp.IQ4_NL, sp.IQ4_XS, sp.F16, sp.BF16):
         assert sp.ggml_supports_mul_mat(*node(t0=t0))
     assert sp.ggml_supports_mul_mat(*node(td=sp.BF16))
     assert sp.ggml_supports_mul_mat(*node(ne12=4, ne02=2))  # broadcast
