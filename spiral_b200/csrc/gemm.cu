@@ -256,23 +256,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (lane == 0) mbar_arrive(&a_full[s]);
         }
       } else {
-      for (int kc = 0; kc < kchunks; ++kc, ++ait) {
-        const int s = ait % kAStages;
-        uint32_t R[CD::kLoads * 4];
+      // The next chunk's packed bytes are loaded one chunk ahead (into Rn)
+      // while this chunk is decoded, so the global-load latency leaves the
+      // path between a free A stage and a full one.
+      uint32_t R[CD::kLoads * 4], Rn[CD::kLoads * 4];
+      auto load_chunk = [&](int kcl, uint32_t (&dst)[CD::kLoads * 4]) {
         if (valid) {
-          const uint4* src = reinterpret_cast<const uint4*>(wrow + static_cast<int64_t>(kc) * CD::kChunkBytes + CD::window(h));
+          const uint4* src =
+              reinterpret_cast<const uint4*>(wrow + static_cast<int64_t>(kcl) * CD::kChunkBytes + CD::window(h));
 #pragma unroll
           for (int i = 0; i < CD::kLoads; ++i) {
             const uint4 v = __ldg(src + i);
-            R[4 * i] = v.x;
-            R[4 * i + 1] = v.y;
-            R[4 * i + 2] = v.z;
-            R[4 * i + 3] = v.w;
+            dst[4 * i] = v.x;
+            dst[4 * i + 1] = v.y;
+            dst[4 * i + 2] = v.z;
+            dst[4 * i + 3] = v.w;
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < CD::kLoads * 4; ++i) R[i] = 0u;
+          for (int i = 0; i < CD::kLoads * 4; ++i) dst[i] = 0u;
         }
+      };
+      load_chunk(0, R);
+      for (int kc = 0; kc < kchunks; ++kc, ++ait) {
+        const int s = ait % kAStages;
+        if (kc + 1 < kchunks) load_chunk(kc + 1, Rn);
         if (!wait(&a_empty[s], ((ait / kAStages) & 1u) ^ 1u)) break;
         tc::fence_after_sync();
         const uint32_t tbase = tmem + (static_cast<uint32_t>(32 * q) << 16) + kAColBase + s * kAStageCols + 64 * h;
@@ -292,6 +300,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[s]);
+#pragma unroll
+        for (int i = 0; i < CD::kLoads * 4; ++i) R[i] = Rn[i];
       }
       }
       if (*abortv) break;
