@@ -460,11 +460,17 @@ static cudaError_t gemm_launch(const MatArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// Tiles of 128 features x 256 tokens, or x 128 tokens when the 256-token
+// tiling leaves SMs idle (e.g. M = 512, N = 4096: 64 tiles on 148 SMs); the
+// narrower tile dequantizes each weight tile twice as often per token but
+// keeps every SM busy.
 cudaError_t gemm(const MatArgs& a, cudaStream_t stream) {
+  const int64_t tiles256 = ((a.M + 255) / 256) * ((a.N + kGemmRows - 1) / kGemmRows);
+  const bool narrow = tiles256 < device_sm_count();
   switch (a.fmt) {
-    case kQ4_0: return gemm_launch<kQ4_0, 256>(a, stream);
-    case kQ8_0: return gemm_launch<kQ8_0, 256>(a, stream);
-    case kQ6_K: return gemm_launch<kQ6_K, 256>(a, stream);
+    case kQ4_0: return narrow ? gemm_launch<kQ4_0, 128>(a, stream) : gemm_launch<kQ4_0, 256>(a, stream);
+    case kQ8_0: return narrow ? gemm_launch<kQ8_0, 128>(a, stream) : gemm_launch<kQ8_0, 256>(a, stream);
+    case kQ6_K: return narrow ? gemm_launch<kQ6_K, 128>(a, stream) : gemm_launch<kQ6_K, 256>(a, stream);
   }
   return cudaErrorInvalidValue;
 }
