@@ -371,13 +371,21 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
   uint8_t* xs = xbuf + grp * 8 * x_pitch;
   const int bar_id = 1 + grp;
   int staged = -1;  // problem whose rows are in xs
+  // The epilogue thread's activation column is the same in every item:
+  // its pair (and routing weight) is read once per problem, not per item.
+  const int my_m = 2 * ((gt >> 2) & 3) + (gt & 1);
+  MoeProblem pr{};
+  int my_pair = 0;
+  float my_wt = 0.f;
   uint32_t it = 0;
   for (int64_t i = i_begin; i < i_end; ++i, ++it) {
     if (static_cast<int>((i - i_begin) % kMoeGroups) != grp) continue;
     const int pidx = static_cast<int>(i / tiles);
     const int tile = static_cast<int>(i % tiles);
-    const MoeProblem pr = probs[pidx];
     if (pidx != staged) {
+      pr = probs[pidx];
+      my_pair = my_m < pr.nx ? pairs[pr.first + my_m] : 0;
+      if constexpr (PHASE == 2) my_wt = my_m < pr.nx ? a.wts[my_pair] : 0.f;
       if constexpr (PHASE == 1) {
         auto src = [&](int m) { return a.x + static_cast<int64_t>(pairs[pr.first + m] / a.topk) * a.x_stride; };
         moe_stage_rows<FMT>(pr.nx, K, src, xs, x_pitch, reinterpret_cast<uint8_t*>(gred), gt, bar_id);
@@ -436,10 +444,9 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
         for (int q = 0; q < wpr; ++q) v += reinterpret_cast<const float*>(&gred[(rbk * wpr + q) * 32 + l])[j];
         const int row = rbk * kTileRows + (l >> 2) + 8 * (j >> 1);
         const int m = 2 * (l & 3) + (j & 1);
-        if (ready && m < pr.nx) {
-          const int pair = pairs[pr.first + m];
+        if (ready && m < pr.nx) {  // m == my_m
           float* part = reinterpret_cast<float*>(a.ws + a.L.part);
-          part[static_cast<int64_t>(pair) * a.H + tile * kItemRows + row] = a.wts[pair] * v;
+          part[static_cast<int64_t>(my_pair) * a.H + tile * kItemRows + row] = my_wt * v;
         }
       }
     } else if (gw < 4) {
@@ -454,16 +461,15 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
       }
       const int row = (l >> 2) + 8 * (j >> 1);
       const int m = 2 * (l & 3) + (j & 1);
-      if (ready && m < pr.nx) {
-        const int pair = pairs[pr.first + m];
+      if (ready && m < pr.nx) {  // m == my_m
         const int feat = tile * kTileRows + row;
         if constexpr (PHASE == 1) {
           uint16_t* h = reinterpret_cast<uint16_t*>(a.ws + a.L.h);
-          h[static_cast<int64_t>(pair) * a.I + feat] =
+          h[static_cast<int64_t>(my_pair) * a.I + feat] =
               static_cast<uint16_t>(pack_bf16x2(silu(v[0]) * v[kAcc - 1], 0.f) & 0xFFFFu);
         } else {
           float* part = reinterpret_cast<float*>(a.ws + a.L.part);
-          part[static_cast<int64_t>(pair) * a.H + feat] = a.wts[pair] * v[0];
+          part[static_cast<int64_t>(my_pair) * a.H + feat] = my_wt * v[0];
         }
       }
     }
