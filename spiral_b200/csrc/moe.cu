@@ -689,6 +689,254 @@ cudaError_t launch_moe_gemv(const MoeArgs& a, cudaStream_t stream) {
                     smem, stream, kargs);
 }
 
+// ------------------------------------------- gate/up, activation-stationary --
+//
+// The gate/up GEMV of the layer with the decode GEMV's structure (gemv_xs.cu)
+// for Q4_0 / Q8_0 at hidden = 16 x 128 x GPW: one CTA per SM, 16 consumer
+// warps and a producer warp.  A work item is (problem, 16 intermediate
+// features); its stage holds the 16 gate and the 16 up rows as 8 + 8 pairs of
+// consecutive rows (pitch 2 rows + 16 bytes; MMA row g <-> row 2g, g + 8 <->
+// 2g + 1).  Warp w owns the K slice [w K/16, (w+1) K/16) of every item; its
+// activation fragments for the current problem's tokens stay in registers
+// (reloaded from a shared staging buffer when the CTA's items move to the
+// next problem) and serve gate and up alike.  The 16 warps' partial gate and
+// up tiles go to 4 reducer warps (rotating per item) through a
+// double-buffered shared array handed over with mbarriers; the reducers sum
+// them in warp order, apply SwiGLU and store h in bf16.
+constexpr int kGuWarps = 16;
+constexpr int kGuThreads = (kGuWarps + 1) * 32;
+constexpr int kGuMaxStages = 8;
+constexpr int kGuReducerWarps = 4;
+constexpr int kGuReducerSets = kGuWarps / kGuReducerWarps;
+constexpr int kGuHeader = 1024;
+constexpr int kGuRedBytes = 2 * kGuWarps * 32 * 32;  // 2 buffers x 16 warps x 32 lanes x (gate, up) float4
+
+template <int FMT, int GPW>
+__global__ void __launch_bounds__(kGuThreads, 1) moe_gateup_xs(const MoeArgs a, int stages, int pair_pitch) {
+  using F = GemvFmt<FMT>;
+  constexpr int kSteps = F::kSteps;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kGuMaxStages;
+  uint64_t* red_full = empty + kGuMaxStages;
+  uint64_t* red_empty = red_full + 2;
+  int& abort_flag = *reinterpret_cast<int*>(smem + 512);
+  float4* red = reinterpret_cast<float4*>(smem + kGuHeader);  // [2][16 warps][32 lanes][gate, up]
+  uint8_t* xbuf = smem + kGuHeader + kGuRedBytes;              // [8 rows][H] bf16
+  const int x_bytes = 8 * a.H * 2;
+  uint8_t* stg = xbuf + x_bytes;
+  const int stage_bytes = 16 * pair_pitch;
+  const int rb = static_cast<int>(a.rb_h);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = a.I / kTileRows;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kGuWarps);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&red_full[b], kGuWarps * 32);
+      mbar_init(&red_empty[b], kGuReducerWarps * 32);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+    griddep_launch_dependents();
+  }
+  __syncthreads();
+  griddep_wait();  // the route kernel wrote what follows
+
+  const int* hdr = reinterpret_cast<const int*>(a.ws + a.L.hdr);
+  const int* pairs = reinterpret_cast<const int*>(a.ws + a.L.pairs);
+  const MoeProblem* probs = reinterpret_cast<const MoeProblem*>(a.ws + a.L.problems);
+  const int64_t items = static_cast<int64_t>(hdr[0]) * tiles;
+  const int64_t i_begin = blockIdx.x * items / gridDim.x, i_end = (blockIdx.x + 1) * items / gridDim.x;
+
+  if (warp == kGuWarps) {
+    // ---------------------------------------------------------- producer --
+    const uint64_t pol = l2_evict_first_policy();
+    uint32_t it = 0;
+    int stage = 0;
+    uint32_t phase = 0u;
+    for (int64_t i = i_begin; i < i_end; ++i, ++it) {
+      const MoeProblem pr = probs[i / tiles];
+      const int tile = static_cast<int>(i % tiles);
+      int go = 0;
+      if (lane == 0) {
+        go = !*(volatile int*)&abort_flag && mbar_wait(&empty[stage], phase ^ 1u);
+        if (go) {
+          mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(rb) * 2 * kTileRows);
+        } else {
+          abort_flag = 1;
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+      if (lane < 16) {
+        // lane q < 8: gate rows 2q, 2q + 1 of the tile; lane 8 + q: up rows
+        const int q = lane & 7;
+        const int64_t row = static_cast<int64_t>(pr.expert) * a.I + tile * kTileRows + 2 * q;
+        const uint8_t* src = (lane < 8 ? a.w_gate : a.w_up) + row * rb;
+        bulk_g2s(stg + stage * stage_bytes + lane * pair_pitch, src, static_cast<uint32_t>(rb) * 2, &full[stage],
+                 pol);
+      }
+      if (++stage == stages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    // Every issued copy must land before the CTA may exit.
+    if (lane == 0) {
+      const uint32_t first = it > static_cast<uint32_t>(stages) ? it - stages : 0u;
+      for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % stages], (j / stages) & 1u);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers --
+  const int r = lane >> 2, c = lane & 3;
+  const bool ftz = a.ftz != 0;
+  const int red_set = warp / kGuReducerWarps;
+  const uint8_t* ra0 = stg + r * pair_pitch + warp * GPW * F::kGroupBytes;
+  uint2 Bx[GPW][kSteps];
+  int staged = -1;
+  MoeProblem pr{};
+  int stage = 0, red_turn = 0;
+  uint32_t phase = 0u;
+  int local = 0;
+  // the reducer thread's output column (the same in every item)
+  const int t_red = (warp % kGuReducerWarps) * 32 + lane;
+  const int l_red = t_red >> 2, j_red = t_red & 3;
+  const int m_red = 2 * (l_red & 3) + (j_red & 1);
+  int pair_red = 0;
+  for (int64_t i = i_begin; i < i_end; ++i, ++local) {
+    const int pidx = static_cast<int>(i / tiles);
+    const int tile = static_cast<int>(i % tiles);
+    if (pidx != staged) {
+      // every warp has its fragments of the previous problem
+      named_bar_sync(1, kGuWarps * 32);
+      pr = probs[pidx];
+      pair_red = m_red < pr.nx ? pairs[pr.first + m_red] : 0;
+      // the problem's activation rows (nx <= 8), 16-byte pieces
+      const int pieces = a.H / 8;
+      for (int q = threadIdx.x; q < pr.nx * pieces; q += kGuWarps * 32) {
+        const int m = q / pieces, pc = q - m * pieces;
+        const int tok = pairs[pr.first + m] / a.topk;
+        reinterpret_cast<uint4*>(xbuf + m * a.H * 2)[pc] =
+            __ldg(reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(tok) * a.x_stride) + pc);
+      }
+      named_bar_sync(1, kGuWarps * 32);
+#pragma unroll
+      for (int g = 0; g < GPW; ++g) {
+#pragma unroll
+        for (int st = 0; st < kSteps; ++st) {
+          const int k = (warp * GPW + g) * F::kGroupK + GroupDecoder<FMT>::xk(st, c);
+          Bx[g][st] = r < pr.nx ? *reinterpret_cast<const uint2*>(xbuf + r * a.H * 2 + k * 2) : make_uint2(0u, 0u);
+        }
+      }
+      staged = pidx;
+    }
+    float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
+    const int s = stage;
+    bool ready = mbar_try_wait(&full[s], phase);
+    if (!ready && !*(volatile int*)&abort_flag) {
+      ready = mbar_wait(&full[s], phase);
+      if (!ready) abort_flag = 1;
+    }
+    if (ready) {
+      const uint8_t* ra = ra0 + s * stage_bytes;
+#pragma unroll
+      for (int g = 0; g < GPW; ++g) {
+        auto bx = [&](int st) { return Bx[g][st]; };
+        const uint8_t* ga = ra + g * F::kGroupBytes;
+        GroupDecoder<FMT>::run_b(ga, ga + rb, c, bx, ftz, accg);
+        const uint8_t* ua = ga + 8 * pair_pitch;
+        GroupDecoder<FMT>::run_b(ua, ua + rb, c, bx, ftz, accu);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (++stage == stages) {
+      stage = 0;
+      phase ^= 1u;
+    }
+
+    // hand the partials to this item's reducers
+    const int rbuf = local & 1;
+    if (local >= 2 && !mbar_try_wait(&red_empty[rbuf], static_cast<uint32_t>((local >> 1) - 1) & 1u) &&
+        !*(volatile int*)&abort_flag) {
+      if (!mbar_wait(&red_empty[rbuf], static_cast<uint32_t>((local >> 1) - 1) & 1u)) abort_flag = 1;
+    }
+    float4* my = red + ((rbuf * kGuWarps + warp) * 32 + lane) * 2;
+    my[0] = make_float4(accg[0], accg[1], accg[2], accg[3]);
+    my[1] = make_float4(accu[0], accu[1], accu[2], accu[3]);
+    mbar_arrive(&red_full[rbuf]);
+    const bool mine = red_turn == red_set;
+    if (++red_turn == kGuReducerSets) red_turn = 0;
+    if (!mine) continue;
+
+    // ---------------------------------------------------- reduction ----
+    if (!mbar_try_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u) && !*(volatile int*)&abort_flag) {
+      if (!mbar_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u)) abort_flag = 1;
+    }
+    const float* rp = reinterpret_cast<const float*>(red + (rbuf * kGuWarps * 32 + l_red) * 2) + j_red;
+    float gsum = 0.f, usum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGuWarps; ++w) {
+      gsum += rp[w * 32 * 8];
+      usum += rp[w * 32 * 8 + 4];
+    }
+    mbar_arrive(&red_empty[rbuf]);
+    const int rowp = (l_red >> 2) + 8 * (j_red >> 1);      // MMA row
+    const int row = rowp < 8 ? 2 * rowp : 2 * (rowp - 8) + 1;  // weight row of the tile
+    if (ready && m_red < pr.nx) {
+      uint16_t* h = reinterpret_cast<uint16_t*>(a.ws + a.L.h);
+      h[static_cast<int64_t>(pair_red) * a.I + tile * kTileRows + row] =
+          static_cast<uint16_t>(pack_bf16x2(silu(gsum) * usum, 0.f) & 0xFFFFu);
+    }
+  }
+}
+
+// GPW (decode groups per warp) of the activation-stationary gate/up, or 0
+// when the layer's shape is not served (then the grouped kernel runs).
+int moe_gu_gpw(const MoeArgs& a) {
+  if (a.fmt != kQ4_0 && a.fmt != kQ8_0) return 0;
+  if (a.H == 2048) return 1;
+  if (a.H == 4096) return 2;
+  return 0;
+}
+
+template <int FMT>
+cudaError_t launch_moe_gateup_xs(const MoeArgs& a, cudaStream_t stream, bool* launched) {
+  *launched = false;
+  const int gpw = moe_gu_gpw(a);
+  if (gpw == 0) return cudaSuccess;
+  // dense rows, 16-byte aligned, for the pair copies
+  if (reinterpret_cast<uintptr_t>(a.w_gate) % 16 || reinterpret_cast<uintptr_t>(a.w_up) % 16 || a.rb_h % 16)
+    return cudaSuccess;
+  const int pair_pitch = 2 * static_cast<int>(a.rb_h) + 16;
+  const size_t fixed = kGuHeader + kGuRedBytes + size_t(8) * a.H * 2;
+  const size_t avail = device_max_smem_optin();
+  const size_t stage = size_t(16) * pair_pitch;
+  if (fixed + 3 * stage > avail) return cudaSuccess;
+  const int stages = static_cast<int>(std::min<size_t>(kGuMaxStages, (avail - fixed) / stage));
+  const size_t smem = fixed + size_t(stages) * stage;
+  auto* kernel = gpw == 1 ? moe_gateup_xs<FMT, 1> : moe_gateup_xs<FMT, 2>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::atomic<bool> configured[64][2];
+  if (!configured[dev & 63][gpw - 1].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(avail));
+    if (e != cudaSuccess) return e;
+    configured[dev & 63][gpw - 1].store(true, std::memory_order_release);
+  }
+  MoeArgs args = a;
+  int st = stages, pp = pair_pitch;
+  void* kargs[] = {&args, &st, &pp};
+  *launched = true;
+  return launch_pdl(reinterpret_cast<const void*>(kernel), dim3(device_sm_count()), dim3(kGuThreads), smem, stream,
+                    kargs);
+}
+
 template <int FMT>
 cudaError_t moe_run(const MoeArgs& a, cudaStream_t stream, const MoeEp* ep = nullptr) {
   MoeArgs args = a;
@@ -699,7 +947,11 @@ cudaError_t moe_run(const MoeArgs& a, cudaStream_t stream, const MoeEp* ep = nul
                                kargs);
     if (e != cudaSuccess) return e;
   }
-  cudaError_t e = launch_moe_gemv<FMT, 1>(a, stream);
+  bool gu_done = false;
+  cudaError_t e = cudaSuccess;
+  if constexpr (FMT == kQ4_0 || FMT == kQ8_0) e = launch_moe_gateup_xs<FMT>(a, stream, &gu_done);
+  if (e != cudaSuccess) return e;
+  if (!gu_done) e = launch_moe_gemv<FMT, 1>(a, stream);
   if (e != cudaSuccess) return e;
   e = launch_moe_gemv<FMT, 2>(a, stream);
   if (e != cudaSuccess) return e;
