@@ -937,6 +937,233 @@ cudaError_t launch_moe_gateup_xs(const MoeArgs& a, cudaStream_t stream, bool* la
                     kargs);
 }
 
+// ---------------------------------------------- down, activation-stationary --
+//
+// The down GEMV (K = inter) with the same structure for Q4_0 / Q8_0 at
+// inter = 6 x 128 (768): a work item is (problem, 64 output rows) copied as
+// 32 pairs of consecutive rows.  12 consumer warps: warp w owns decode group
+// g = w % 6 of K and the row blocks 2 (w / 6) and 2 (w / 6) + 1 of the item,
+// so its activation fragments (the problem's h rows, one group) stay in
+// registers and every warp issues 16 MMAs per item.  4 reducer warps
+// (rotating over 3 sets) sum each output's 6 group partials in order and
+// store w_{t,j} * y into the per-pair outputs.
+constexpr int kDnGroups = 6;
+constexpr int kDnWarps = 12;
+constexpr int kDnThreads = (kDnWarps + 1) * 32;
+constexpr int kDnMaxStages = 12;
+constexpr int kDnReducerWarps = 4;
+constexpr int kDnReducerSets = kDnWarps / kDnReducerWarps;
+constexpr int kDnItemRows = 64;
+constexpr int kDnHeader = 1024;
+constexpr int kDnRedBytes = 2 * kDnWarps * 32 * 32;  // 2 buffers x 12 warps x 32 lanes x 2 float4
+
+template <int FMT>
+__global__ void __launch_bounds__(kDnThreads, 1) moe_down_xs(const MoeArgs a, int stages, int pair_pitch) {
+  using F = GemvFmt<FMT>;
+  constexpr int kSteps = F::kSteps;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kDnMaxStages;
+  uint64_t* red_full = empty + kDnMaxStages;
+  uint64_t* red_empty = red_full + 2;
+  int& abort_flag = *reinterpret_cast<int*>(smem + 512);
+  float4* red = reinterpret_cast<float4*>(smem + kDnHeader);  // [2][12 warps][32 lanes][2 row blocks]
+  uint8_t* xbuf = smem + kDnHeader + kDnRedBytes;             // [8 rows][I] bf16
+  uint8_t* stg = xbuf + 8 * a.I * 2;
+  const int stage_bytes = (kDnItemRows / 2) * pair_pitch;
+  const int rb = static_cast<int>(a.rb_i);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = a.H / kDnItemRows;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kDnWarps);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&red_full[b], kDnWarps * 32);
+      mbar_init(&red_empty[b], kDnReducerWarps * 32);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+    griddep_launch_dependents();
+  }
+  __syncthreads();
+  griddep_wait();  // the gate/up kernel wrote h
+
+  const int* hdr = reinterpret_cast<const int*>(a.ws + a.L.hdr);
+  const int* pairs = reinterpret_cast<const int*>(a.ws + a.L.pairs);
+  const MoeProblem* probs = reinterpret_cast<const MoeProblem*>(a.ws + a.L.problems);
+  const uint16_t* hbuf = reinterpret_cast<const uint16_t*>(a.ws + a.L.h);
+  const int64_t items = static_cast<int64_t>(hdr[0]) * tiles;
+  const int64_t i_begin = blockIdx.x * items / gridDim.x, i_end = (blockIdx.x + 1) * items / gridDim.x;
+
+  if (warp == kDnWarps) {
+    // ---------------------------------------------------------- producer --
+    const uint64_t pol = l2_evict_first_policy();
+    uint32_t it = 0;
+    int stage = 0;
+    uint32_t phase = 0u;
+    for (int64_t i = i_begin; i < i_end; ++i, ++it) {
+      const MoeProblem pr = probs[i / tiles];
+      const int tile = static_cast<int>(i % tiles);
+      int go = 0;
+      if (lane == 0) {
+        go = !*(volatile int*)&abort_flag && mbar_wait(&empty[stage], phase ^ 1u);
+        if (go) {
+          mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(rb) * kDnItemRows);
+        } else {
+          abort_flag = 1;
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+      // lane q: rows 2q, 2q + 1 of the item
+      const int64_t row = static_cast<int64_t>(pr.expert) * a.H + tile * kDnItemRows + 2 * lane;
+      bulk_g2s(stg + stage * stage_bytes + lane * pair_pitch, a.w_down + row * rb, static_cast<uint32_t>(rb) * 2,
+               &full[stage], pol);
+      if (++stage == stages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    if (lane == 0) {
+      const uint32_t first = it > static_cast<uint32_t>(stages) ? it - stages : 0u;
+      for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % stages], (j / stages) & 1u);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers --
+  const int r = lane >> 2, c = lane & 3;
+  const bool ftz = a.ftz != 0;
+  const int g = warp % kDnGroups, rbp = warp / kDnGroups;  // decode group, row-block pair
+  const int red_set = warp / kDnReducerWarps;
+  // MMA row r of row block b = pair 8b + r (weight rows 16b + 2r, +1)
+  const uint8_t* ra0 = stg + (16 * rbp + r) * pair_pitch + g * F::kGroupBytes;
+  uint2 Bx[kSteps];
+  int staged = -1;
+  MoeProblem pr{};
+  int stage = 0, red_turn = 0;
+  uint32_t phase = 0u;
+  int local = 0;
+  const int t_red = (warp % kDnReducerWarps) * 32 + lane;
+  const int l_red = t_red >> 2, j_red = t_red & 3;
+  const int m_red = 2 * (l_red & 3) + (j_red & 1);
+  int pair_red = 0;
+  float wt_red = 0.f;
+  for (int64_t i = i_begin; i < i_end; ++i, ++local) {
+    const int pidx = static_cast<int>(i / tiles);
+    const int tile = static_cast<int>(i % tiles);
+    if (pidx != staged) {
+      named_bar_sync(1, kDnWarps * 32);
+      pr = probs[pidx];
+      pair_red = m_red < pr.nx ? pairs[pr.first + m_red] : 0;
+      wt_red = m_red < pr.nx ? a.wts[pair_red] : 0.f;
+      const int pieces = a.I / 8;
+      for (int q = threadIdx.x; q < pr.nx * pieces; q += kDnWarps * 32) {
+        const int m = q / pieces, pc = q - m * pieces;
+        reinterpret_cast<uint4*>(xbuf + m * a.I * 2)[pc] =
+            __ldg(reinterpret_cast<const uint4*>(hbuf + static_cast<int64_t>(pairs[pr.first + m]) * a.I) + pc);
+      }
+      named_bar_sync(1, kDnWarps * 32);
+#pragma unroll
+      for (int st = 0; st < kSteps; ++st) {
+        const int k = g * F::kGroupK + GroupDecoder<FMT>::xk(st, c);
+        Bx[st] = r < pr.nx ? *reinterpret_cast<const uint2*>(xbuf + r * a.I * 2 + k * 2) : make_uint2(0u, 0u);
+      }
+      staged = pidx;
+    }
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+    const int s = stage;
+    bool ready = mbar_try_wait(&full[s], phase);
+    if (!ready && !*(volatile int*)&abort_flag) {
+      ready = mbar_wait(&full[s], phase);
+      if (!ready) abort_flag = 1;
+    }
+    if (ready) {
+      auto bx = [&](int st) { return Bx[st]; };
+      const uint8_t* b0 = ra0 + s * stage_bytes;
+      GroupDecoder<FMT>::run_b(b0, b0 + rb, c, bx, ftz, acc0);
+      const uint8_t* b1 = b0 + 8 * pair_pitch;
+      GroupDecoder<FMT>::run_b(b1, b1 + rb, c, bx, ftz, acc1);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (++stage == stages) {
+      stage = 0;
+      phase ^= 1u;
+    }
+
+    const int rbuf = local & 1;
+    if (local >= 2 && !mbar_try_wait(&red_empty[rbuf], static_cast<uint32_t>((local >> 1) - 1) & 1u) &&
+        !*(volatile int*)&abort_flag) {
+      if (!mbar_wait(&red_empty[rbuf], static_cast<uint32_t>((local >> 1) - 1) & 1u)) abort_flag = 1;
+    }
+    float4* my = red + ((rbuf * kDnWarps + warp) * 32 + lane) * 2;
+    my[0] = make_float4(acc0[0], acc0[1], acc0[2], acc0[3]);
+    my[1] = make_float4(acc1[0], acc1[1], acc1[2], acc1[3]);
+    mbar_arrive(&red_full[rbuf]);
+    const bool mine = red_turn == red_set;
+    if (++red_turn == kDnReducerSets) red_turn = 0;
+    if (!mine) continue;
+
+    // ---------------------------------------------------- reduction ----
+    if (!mbar_try_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u) && !*(volatile int*)&abort_flag) {
+      if (!mbar_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u)) abort_flag = 1;
+    }
+    float v[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {  // row block b of the item: warps (b / 2) * 6 + g, accumulator b % 2
+      const float* rp = reinterpret_cast<const float*>(red + ((rbuf * kDnWarps + (b >> 1) * kDnGroups) * 32 + l_red) * 2 +
+                                                       (b & 1)) +
+                        j_red;
+      float sum = 0.f;
+#pragma unroll
+      for (int gg = 0; gg < kDnGroups; ++gg) sum += rp[gg * 32 * 8];
+      v[b] = sum;
+    }
+    mbar_arrive(&red_empty[rbuf]);
+    if (ready && m_red < pr.nx) {
+      const int rowp = (l_red >> 2) + 8 * (j_red >> 1);
+      const int row16 = rowp < 8 ? 2 * rowp : 2 * (rowp - 8) + 1;
+      float* part = reinterpret_cast<float*>(a.ws + a.L.part) + static_cast<int64_t>(pair_red) * a.H +
+                    tile * kDnItemRows + row16;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) part[16 * b] = wt_red * v[b];
+    }
+  }
+}
+
+template <int FMT>
+cudaError_t launch_moe_down_xs(const MoeArgs& a, cudaStream_t stream, bool* launched) {
+  *launched = false;
+  if (a.fmt != kQ4_0 && a.fmt != kQ8_0) return cudaSuccess;
+  if (a.I != kDnGroups * GemvFmt<FMT>::kGroupK || a.H % kDnItemRows != 0) return cudaSuccess;
+  if (reinterpret_cast<uintptr_t>(a.w_down) % 16 || a.rb_i % 16) return cudaSuccess;
+  const int pair_pitch = 2 * static_cast<int>(a.rb_i) + 16;
+  const size_t fixed = kDnHeader + kDnRedBytes + size_t(8) * a.I * 2;
+  const size_t avail = device_max_smem_optin();
+  const size_t stage = size_t(kDnItemRows / 2) * pair_pitch;
+  if (fixed + 3 * stage > avail) return cudaSuccess;
+  const int stages = static_cast<int>(std::min<size_t>(kDnMaxStages, (avail - fixed) / stage));
+  const size_t smem = fixed + size_t(stages) * stage;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::atomic<bool> configured[64];
+  if (!configured[dev & 63].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(moe_down_xs<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(avail));
+    if (e != cudaSuccess) return e;
+    configured[dev & 63].store(true, std::memory_order_release);
+  }
+  MoeArgs args = a;
+  int st = stages, pp = pair_pitch;
+  void* kargs[] = {&args, &st, &pp};
+  *launched = true;
+  return launch_pdl(reinterpret_cast<const void*>(moe_down_xs<FMT>), dim3(device_sm_count()), dim3(kDnThreads), smem,
+                    stream, kargs);
+}
+
 template <int FMT>
 cudaError_t moe_run(const MoeArgs& a, cudaStream_t stream, const MoeEp* ep = nullptr) {
   MoeArgs args = a;
@@ -953,7 +1180,10 @@ cudaError_t moe_run(const MoeArgs& a, cudaStream_t stream, const MoeEp* ep = nul
   if (e != cudaSuccess) return e;
   if (!gu_done) e = launch_moe_gemv<FMT, 1>(a, stream);
   if (e != cudaSuccess) return e;
-  e = launch_moe_gemv<FMT, 2>(a, stream);
+  bool dn_done = false;
+  if constexpr (FMT == kQ4_0 || FMT == kQ8_0) e = launch_moe_down_xs<FMT>(a, stream, &dn_done);
+  if (e != cudaSuccess) return e;
+  if (!dn_done) e = launch_moe_gemv<FMT, 2>(a, stream);
   if (e != cudaSuccess) return e;
   const int64_t total = static_cast<int64_t>(a.T) * a.H;
   if (ep != nullptr) {
