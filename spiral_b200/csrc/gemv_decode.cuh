@@ -1,15 +1,26 @@
 // gemv_decode.cuh — register-level decoders that feed mma.sync.m16n8k16 A
 // fragments straight from canonical GGUF blocks in shared memory, shared by
-// the decode GEMV (gemv.cu) and the MoE expert GEMVs (moe.cu).
+// the decode GEMV (gemv.cu, gemv_xs.cu) and the MoE expert GEMVs (moe.cu).
 //
-// Dequantization is exact: a quant byte is placed in the mantissa of an fp32
-// with one byte permute, f = 1 + q*2^-s, and one fused multiply-add computes
-// f*(2^s*d) - (2^s + bias)*d = (q - bias)*d.  Both constants are exact in
-// fp32 (at most 24 significant bits) and so is the result, so the FMA does
-// not round; cvt.rn.bf16x2.f32 then rounds once to nearest even.  The A
-// fragments therefore hold exactly the bf16 weights of the standalone
-// dequant (bf16_rne(d*int), up to the sign of a zero weight, which cannot
-// change a dot product).  Pairs of weights go through one fma.rn.f32x2.
+// Dequantization is exact, by one of two routes.
+//  * Q4_0 / Q8_0 (fp16 route): one LOP3 puts two quants into the mantissas of
+//    an fp16 pair, u = 2^e + q (q a nibble at bits 0-3 with 0x6400 = 1024, a
+//    nibble at bits 4-7 with 0x5400 = 64 (mantissa unit 2^-4), or a byte with
+//    its sign bit flipped at bits 0-7 with 0x6400); one mixed-precision
+//    fma.rn.f32.f16 per weight computes u*d - (2^e + bias)*d with the fp16
+//    scale d itself as the other operand.  The product u*d is exact inside
+//    the FMA, the bias product (2^e + bias)*d has at most 19 significant bits
+//    and the result (q - bias)*d at most 19, so the FMA does not round.
+//  * Q6_K (fp32 route): a 6-bit quant with bit 7 set goes into an fp32
+//    mantissa with one byte permute, f = 1 + q*2^-7, and one fma.rn.f32x2
+//    per pair computes f*(128 ds) - 160 ds with ds = d*sc (at most 19 bits):
+//    exact again.  (ds does not fit an fp16 operand.)
+// cvt.rn.bf16x2.f32 then rounds once to nearest even, so the A fragments hold
+// exactly the bf16 weights of the standalone dequant (bf16_rne(d*int), up to
+// the sign of a zero weight, which cannot change a dot product).  The fp16
+// route costs 10 integer-pipe instructions per MMA against 15 for a byte
+// permute per weight, which matters because the decode, not HBM, bounds
+// these kernels.
 #pragma once
 
 #include "common.cuh"
@@ -57,16 +68,47 @@ __device__ __forceinline__ uint64_t dup2(float v) {
   return (b << 32) | b;
 }
 
-// Byte i of w into bits 8..15 of 0x3F80_00_00: f = 1 + byte * 2^-15.
-template <int I>
-__device__ __forceinline__ uint32_t byte_to_f1(uint32_t w) {
-  return __byte_perm(w, 0x3F800000u, 0x7604u | (I << 4));
-}
 // Byte i of w (its bit 7 set) into bits 16..23 of 0x3F_00_00_00:
 // f = 1 + (byte & 0x7f) * 2^-7.
 template <int I>
 __device__ __forceinline__ uint32_t byte_to_f2(uint32_t w) {
   return __byte_perm(w, 0x3F000000u, 0x7054u | (I << 8));
+}
+
+// (a & m) | o and (a & m) ^ o in one LOP3 each.
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t o) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(m), "r"(o));
+  return r;
+}
+__device__ __forceinline__ uint32_t lop_and_xor(uint32_t a, uint32_t m, uint32_t o) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(a), "r"(m), "r"(o));
+  return r;
+}
+// u.lo * d + c and u.hi * d + c for the fp16 pair u and the fp16 scale d,
+// in fp32 with one rounding.
+__device__ __forceinline__ float fmah_lo(uint32_t u, unsigned short d, float c) {
+  float r;
+  asm("{ .reg .b16 l, h; mov.b32 {l, h}, %1; fma.rn.f32.f16 %0, l, %2, %3; }" : "=f"(r) : "r"(u), "h"(d), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float fmah_hi(uint32_t u, unsigned short d, float c) {
+  float r;
+  asm("{ .reg .b16 l, h; mov.b32 {l, h}, %1; fma.rn.f32.f16 %0, h, %2, %3; }" : "=f"(r) : "r"(u), "h"(d), "f"(c));
+  return r;
+}
+// The fp16 scale operand: a subnormal scale becomes +0 under ftz, as
+// fp16_bits_to_f32 flushes it.
+__device__ __forceinline__ unsigned short fp16_scale_bits(uint32_t h, bool ftz) {
+  return (ftz && (h & 0x7c00u) == 0u) ? static_cast<unsigned short>(0) : static_cast<unsigned short>(h);
+}
+// Two weights of the fp16 route, rounded to one bf16 pair (x in the low half).
+__device__ __forceinline__ uint32_t h2pack_lo(uint32_t ux, uint32_t uy, unsigned short d, float c) {
+  return pack_bf16x2(fmah_lo(ux, d, c), fmah_lo(uy, d, c));
+}
+__device__ __forceinline__ uint32_t h2pack_hi(uint32_t ux, uint32_t uy, unsigned short d, float c) {
+  return pack_bf16x2(fmah_hi(ux, d, c), fmah_hi(uy, d, c));
 }
 
 // --------------------------------------------- per-format group decoders --
@@ -110,36 +152,32 @@ struct GroupDecoder<kQ4_0> {
         qb[j] = __funnelshift_r(wb[j], wb[j + 1], sh);
       }
     }
-    const float da = fp16_bits_to_f32(lds_u16(ra + 18 * c), ftz);
-    const float db = fp16_bits_to_f32(lds_u16(rb + 18 * c), ftz);
-    // low nibble: f = 1 + q 2^-15; high nibble (16q in the byte): 1 + q 2^-11.
-    // 2^15 + 8 = 8 * 4097 and 2^11 + 8 = 8 * 257 keep the bias products exact.
-    const uint64_t DLa = dup2(da * 32768.0f), CLa = dup2(da * -32776.0f);
-    const uint64_t DHa = dup2(da * 2048.0f), CHa = dup2(da * -2056.0f);
-    const uint64_t DLb = dup2(db * 32768.0f), CLb = dup2(db * -32776.0f);
-    const uint64_t DHb = dup2(db * 2048.0f), CHb = dup2(db * -2056.0f);
+    const unsigned short ha = fp16_scale_bits(lds_u16(ra + 18 * c), ftz);
+    const unsigned short hb = fp16_scale_bits(lds_u16(rb + 18 * c), ftz);
+    const float da = fp16_bits_to_f32(ha, false), db = fp16_bits_to_f32(hb, false);
+    // low nibble: u = 1024 + q, bias 1032 = 8 * 129; high nibble (bits 4-7
+    // under 0x5400): u = 64 + q, bias 72
+    const float CLa = da * -1032.0f, CHa = da * -72.0f, CLb = db * -1032.0f, CHb = db * -72.0f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint32_t la = qa[j] & 0x0F0F0F0Fu, ha = qa[j] & 0xF0F0F0F0u;
-      const uint32_t lb = qb[j] & 0x0F0F0F0Fu, hb = qb[j] & 0xF0F0F0F0u;
+      // bytes 0 and 2 of the word in u02, bytes 1 and 3 in u13
+      const uint32_t a8 = qa[j] >> 8, b8 = qb[j] >> 8;
+      const uint32_t la02 = lop_and_or(qa[j], 0x000F000Fu, 0x64006400u), la13 = lop_and_or(a8, 0x000F000Fu, 0x64006400u);
+      const uint32_t lb02 = lop_and_or(qb[j], 0x000F000Fu, 0x64006400u), lb13 = lop_and_or(b8, 0x000F000Fu, 0x64006400u);
       const uint2 b0 = bx(2 * j);
-      mma_bf16_16816(acc, fma2_pack(byte_to_f1<0>(la), byte_to_f1<1>(la), DLa, CLa),
-                     fma2_pack(byte_to_f1<0>(lb), byte_to_f1<1>(lb), DLb, CLb),
-                     fma2_pack(byte_to_f1<2>(la), byte_to_f1<3>(la), DLa, CLa),
-                     fma2_pack(byte_to_f1<2>(lb), byte_to_f1<3>(lb), DLb, CLb), b0.x, b0.y);
+      mma_bf16_16816(acc, h2pack_lo(la02, la13, ha, CLa), h2pack_lo(lb02, lb13, hb, CLb), h2pack_hi(la02, la13, ha, CLa),
+                     h2pack_hi(lb02, lb13, hb, CLb), b0.x, b0.y);
+      const uint32_t ua02 = lop_and_or(qa[j], 0x00F000F0u, 0x54005400u), ua13 = lop_and_or(a8, 0x00F000F0u, 0x54005400u);
+      const uint32_t ub02 = lop_and_or(qb[j], 0x00F000F0u, 0x54005400u), ub13 = lop_and_or(b8, 0x00F000F0u, 0x54005400u);
       const uint2 b1 = bx(2 * j + 1);
-      mma_bf16_16816(acc, fma2_pack(byte_to_f1<0>(ha), byte_to_f1<1>(ha), DHa, CHa),
-                     fma2_pack(byte_to_f1<0>(hb), byte_to_f1<1>(hb), DHb, CHb),
-                     fma2_pack(byte_to_f1<2>(ha), byte_to_f1<3>(ha), DHa, CHa),
-                     fma2_pack(byte_to_f1<2>(hb), byte_to_f1<3>(hb), DHb, CHb), b1.x, b1.y);
+      mma_bf16_16816(acc, h2pack_lo(ua02, ua13, ha, CHa), h2pack_lo(ub02, ub13, hb, CHb), h2pack_hi(ua02, ua13, ha, CHa),
+                     h2pack_hi(ub02, ub13, hb, CHb), b1.x, b1.y);
     }
   }
   __host__ __device__ __forceinline__ static int xk(int s, int c) { return 32 * c + 16 * (s & 1) + 4 * (s >> 1); }
 };
 
 // Q8_0: lane c owns block c (34 bytes at 34c); step s = weights 4s..4s+3.
-// int8 q is biased to u = q + 128 (x ^ 0x80); f = 1 + u 2^-15 and
-// 2^15 + 128 = 128 * 257 keeps the bias product exact.
 template <>
 struct GroupDecoder<kQ8_0> {
   __device__ __forceinline__ static void run(const uint8_t* ra, const uint8_t* rb, int c, const uint8_t* xg, bool ftz,
@@ -151,23 +189,22 @@ struct GroupDecoder<kQ8_0> {
                                                float (&acc)[4]) {
     const int woff = 34 * c + 2 * (c & 1);
     const uint32_t sh = (c & 1) ? 0u : 16u;
-    const float da = fp16_bits_to_f32(lds_u16(ra + 34 * c), ftz);
-    const float db = fp16_bits_to_f32(lds_u16(rb + 34 * c), ftz);
-    const uint64_t Da = dup2(da * 32768.0f), Ca = dup2(da * -32896.0f);
-    const uint64_t Db = dup2(db * 32768.0f), Cb = dup2(db * -32896.0f);
+    // u = 1024 + (q + 128) (the byte with its sign bit flipped), bias 1152 = 128 * 9
+    const unsigned short ha = fp16_scale_bits(lds_u16(ra + 34 * c), ftz);
+    const unsigned short hb = fp16_scale_bits(lds_u16(rb + 34 * c), ftz);
+    const float Ca = fp16_bits_to_f32(ha, false) * -1152.0f, Cb = fp16_bits_to_f32(hb, false) * -1152.0f;
     uint32_t pa = lds32(ra + woff), pb = lds32(rb + woff);
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
       const uint32_t na = lds32(ra + woff + 4 * (s + 1)), nb = lds32(rb + woff + 4 * (s + 1));
-      const uint32_t qa = __funnelshift_r(pa, na, sh) ^ 0x80808080u;
-      const uint32_t qb = __funnelshift_r(pb, nb, sh) ^ 0x80808080u;
+      const uint32_t qa = __funnelshift_r(pa, na, sh), qb = __funnelshift_r(pb, nb, sh);
       pa = na;
       pb = nb;
+      const uint32_t a02 = lop_and_xor(qa, 0x00FF00FFu, 0x64806480u), a13 = lop_and_xor(qa >> 8, 0x00FF00FFu, 0x64806480u);
+      const uint32_t b02 = lop_and_xor(qb, 0x00FF00FFu, 0x64806480u), b13 = lop_and_xor(qb >> 8, 0x00FF00FFu, 0x64806480u);
       const uint2 b = bx(s);
-      mma_bf16_16816(acc, fma2_pack(byte_to_f1<0>(qa), byte_to_f1<1>(qa), Da, Ca),
-                     fma2_pack(byte_to_f1<0>(qb), byte_to_f1<1>(qb), Db, Cb),
-                     fma2_pack(byte_to_f1<2>(qa), byte_to_f1<3>(qa), Da, Ca),
-                     fma2_pack(byte_to_f1<2>(qb), byte_to_f1<3>(qb), Db, Cb), b.x, b.y);
+      mma_bf16_16816(acc, h2pack_lo(a02, a13, ha, Ca), h2pack_lo(b02, b13, hb, Cb), h2pack_hi(a02, a13, ha, Ca),
+                     h2pack_hi(b02, b13, hb, Cb), b.x, b.y);
     }
   }
   __host__ __device__ __forceinline__ static int xk(int s, int c) { return 32 * c + 4 * s; }
