@@ -23,9 +23,11 @@
 //    (bf16, the exact inputs: nothing is converted).  Per tile the warp
 //    decodes its slice with the exact decoders of gemv_decode.cuh (A
 //    fragments hold bf16_rne(d * q), bit for bit the standalone dequant) and
-//    the 16 warps' partial 16x8 tiles are summed in warp order by 4 reducer
-//    warps (rotating per tile) through a double-buffered shared array, handed
-//    over with mbarriers, so decoding warps never wait for a reduction.
+//    the 16 warps' partial 16x8 tiles are summed in warp order by a reducer
+//    warp of its own through a double-buffered shared array, handed over with
+//    mbarriers, so decoding warps never wait for a reduction (reductions done
+//    by rotating sets of the decoding warps cost about 0.3 us per tile: the
+//    tile's last partial waited for the previous tile's reducers).
 // The summation order depends on K alone, so every row gets the same bits
 // whatever its position, shard or tile count (the row-sharded call with the
 // all-gather fused in equals the single-GPU call bit for bit).
@@ -39,14 +41,13 @@ namespace spiral {
 namespace {
 
 constexpr int kXsWarps = 16;  // consumer warps: warp w owns K slice w
-constexpr int kXsThreads = (kXsWarps + 1) * 32;  // + the producer warp
+constexpr int kXsWarpProducer = kXsWarps, kXsWarpReducer = kXsWarps + 1;
+constexpr int kXsThreads = (kXsWarps + 2) * 32;  // + the producer and the reducer warp
 constexpr int kXsRows = 16;  // tile height (MMA M)
 constexpr int kXsMaxStages = 8;
-constexpr int kXsReducerWarps = 4;  // 128 threads: one output each
-constexpr int kXsReducerSets = kXsWarps / kXsReducerWarps;
 constexpr int kXsHeader = 2048;  // barriers and abort word; gathered-tile staging at 1024
 constexpr int kXsRedBytes = 2 * kXsWarps * 32 * 16;
-constexpr int kXsBarConsumers = 1 + kXsReducerSets;  // named barrier of the consumer warps
+constexpr int kXsBarConsumers = 1;  // named barrier of the consumer warps
 
 struct XsParams {
   const uint8_t* w;
@@ -89,7 +90,10 @@ __device__ __forceinline__ bool xs_wait(uint64_t* bar, uint32_t parity, int& abo
 __device__ __forceinline__ int xs_weight_row(int R) { return R < 8 ? 2 * R : 2 * (R - 8) + 1; }
 
 template <int FMT, int GPW, bool GATHER, bool FTZ>
-__global__ void __launch_bounds__(kXsThreads, 1) gemv_xs_kernel(const XsParams p) {
+// 18 warps are spread 5 + 5 + 4 + 4 over the sub-partitions, each with a
+// quarter of the register file: 96 registers per thread is the most that
+// launches.
+__global__ void __maxnreg__(96) gemv_xs_kernel(const XsParams p) {
   using F = GemvFmt<FMT>;
   constexpr int kSteps = F::kSteps;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -114,7 +118,7 @@ __global__ void __launch_bounds__(kXsThreads, 1) gemv_xs_kernel(const XsParams p
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&red_full[b], kXsWarps * 32);
-      mbar_init(&red_empty[b], kXsReducerWarps * 32);
+      mbar_init(&red_empty[b], 32);
     }
     mbar_init(xready, kXsWarps);
     abort_flag = 0;
@@ -123,7 +127,7 @@ __global__ void __launch_bounds__(kXsThreads, 1) gemv_xs_kernel(const XsParams p
   }
   __syncthreads();
 
-  if (warp == kXsWarps) {
+  if (warp == kXsWarpProducer) {
     // ---------------------------------------------------------- producer --
     // tile `it` of this CTA into stage it % stages, once every consumer warp
     // has finished the tile that used that stage before
@@ -177,6 +181,85 @@ __global__ void __launch_bounds__(kXsThreads, 1) gemv_xs_kernel(const XsParams p
   if constexpr (GATHER) calls = *reinterpret_cast<volatile const uint32_t*>(p.xchg_peers[p.rank]);
   const int r = lane >> 2, c = lane & 3;
 
+  const int ntiles = static_cast<int>(tiles);
+  if (warp == kXsWarpReducer) {
+    // ---------------------------------------------------------- reducer --
+    // Lane l sums the 16 warps' float4 partials of fragment lane l in warp
+    // order: outputs (rows r, r + 8 of MMA row r = l / 4) x (vectors
+    // 2 (l % 4), + 1).
+    uint16_t* tile_out = reinterpret_cast<uint16_t*>(smem + 1024);  // [8][16] bf16
+    for (int tile = blockIdx.x, local = 0; tile < ntiles; tile += gridDim.x, ++local) {
+      const int rbuf = local & 1;
+      xs_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u, abort_flag);
+      const float4* rp = red + rbuf * kXsWarps * 32 + lane;
+      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int w = 0; w < kXsWarps; ++w) {
+        const float4 v = rp[w * 32];
+        sum.x += v.x;
+        sum.y += v.y;
+        sum.z += v.z;
+        sum.w += v.w;
+      }
+      mbar_arrive(&red_empty[rbuf]);
+      const float sums[4] = {sum.x, sum.y, sum.z, sum.w};
+      if constexpr (GATHER) {
+        // the tile's bf16 outputs, [m][16 rows], then 16-byte pieces to the
+        // local output and flagged unit pairs to every other rank's slot
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int row = xs_weight_row((lane >> 2) + 8 * (j >> 1));
+          const int m = 2 * (lane & 3) + (j & 1);
+          tile_out[m * kXsRows + row] = static_cast<uint16_t>(pack_bf16x2(sums[j], 0.f) & 0xFFFFu);
+        }
+        __syncwarp();
+        const int64_t r0 = static_cast<int64_t>(tile) * kXsRows;
+        const int local_items = p.M * 2;
+        const int items = *(volatile int*)&abort_flag ? local_items : local_items + p.M * 4 * (p.world - 1);
+        for (int q = lane; q < items; q += 32) {
+          if (q < local_items) {
+            const int half = q & 1, mm = q >> 1;
+            if (r0 + half * 8 + 8 > p.N) continue;
+            *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + static_cast<int64_t>(mm) * p.y_sm + p.n_offset +
+                                      r0 + half * 8) = *reinterpret_cast<const uint4*>(tile_out + mm * kXsRows + half * 8);
+          } else {
+            const int qq = q - local_items;
+            const int piece = qq & 3, mm = (qq >> 2) % p.M, k = (qq >> 2) / p.M;
+            if (r0 + piece * 4 + 4 > p.N) continue;
+            const int rr = k < p.rank ? k : k + 1;
+            const uint2 d = *reinterpret_cast<const uint2*>(tile_out + mm * kXsRows + piece * 4);
+            const uint64_t hi = static_cast<uint64_t>(xchg_flag_xs(calls)) << 32;
+            const int64_t col = p.n_offset + r0 + piece * 4;
+            uint8_t* dst = p.xchg_peers[rr] + kGemvXchgCtrlBytes + (calls & 1) * gemv_xchg_slot_bytes(p.n_total) +
+                           mm * 4 * p.n_total + col * 4;
+            asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(hi | d.x), "l"(hi | d.y)
+                         : "memory");
+          }
+        }
+        __syncwarp();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int row = xs_weight_row((lane >> 2) + 8 * (j >> 1));
+          const int m = 2 * (lane & 3) + (j & 1);
+          const int64_t n = static_cast<int64_t>(tile) * kXsRows + row;
+          if (m < p.M && n < p.N) {
+            const int64_t off = (n >> 3) * p.y_s8 + static_cast<int64_t>(m) * p.y_sm + (n & 7);
+            if (p.y_bf16) {
+              static_cast<uint16_t*>(p.y)[off] = static_cast<uint16_t>(pack_bf16x2(sums[j], 0.f) & 0xFFFFu);
+            } else if (p.accumulate) {
+              static_cast<float*>(p.y)[off] += sums[j];
+            } else {
+              static_cast<float*>(p.y)[off] = sums[j];
+            }
+          }
+        }
+      }
+    }
+    return;
+  }
+
+
   // This warp's activation fragments: for its groups g (global index
   // warp * GPW + g) and steps s, lane (r, c) holds x[r][4 consecutive k at
   // group start + xk(s, c)] (bf16x4) for vector r < M, zero otherwise.  Two
@@ -219,12 +302,9 @@ __global__ void __launch_bounds__(kXsThreads, 1) gemv_xs_kernel(const XsParams p
     if (lane == 0) mbar_arrive(xready);
   }
 
-  const int red_set = warp / kXsReducerWarps;
-  uint16_t* tile_out = reinterpret_cast<uint16_t*>(smem + 1024) + red_set * (8 * kXsRows);
   // MMA row r = weight row 2r (pair r, first row); row r + 8 = 2r + 1
   const uint8_t* ra0 = stages + r * p.pair_pitch + warp * GPW * F::kGroupBytes;
-  const int ntiles = static_cast<int>(tiles);
-  int stage = 0, red_turn = 0;
+  int stage = 0;
   uint32_t phase = 0u;
   for (int tile = blockIdx.x, local = 0; tile < ntiles; tile += gridDim.x, ++local) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -252,67 +332,11 @@ __global__ void __launch_bounds__(kXsThreads, 1) gemv_xs_kernel(const XsParams p
       phase ^= 1u;
     }
 
-    // hand the partial to this tile's reducers
+    // hand the partial to the reducer warp
     const int rbuf = local & 1;
     if (local >= 2) xs_wait(&red_empty[rbuf], static_cast<uint32_t>((local >> 1) - 1) & 1u, abort_flag);
     red[(rbuf * kXsWarps + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
     mbar_arrive(&red_full[rbuf]);
-    const bool mine = red_turn == red_set;
-    if (++red_turn == kXsReducerSets) red_turn = 0;
-    if (!mine) continue;
-
-    // --------------------------------------------------- reduction ----
-    xs_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u, abort_flag);
-    const int t = (warp % kXsReducerWarps) * 32 + lane;  // 0..127: one output each
-    const int l = t >> 2, j = t & 3;
-    const float* rp = reinterpret_cast<const float*>(red + rbuf * kXsWarps * 32 + l) + j;
-    float sum = 0.f;
-#pragma unroll
-    for (int w = 0; w < kXsWarps; ++w) sum += rp[w * 32 * 4];
-    mbar_arrive(&red_empty[rbuf]);
-    const int row = xs_weight_row((l >> 2) + 8 * (j >> 1));
-    const int m = 2 * (l & 3) + (j & 1);
-    const int64_t n = static_cast<int64_t>(tile) * kXsRows + row;
-    if constexpr (GATHER) {
-      // the tile's bf16 outputs, [m][16 rows], then 16-byte pieces to the
-      // local output and flagged unit pairs to every other rank's slot
-      const int bar = 1 + red_set;
-      tile_out[m * kXsRows + row] = static_cast<uint16_t>(pack_bf16x2(sum, 0.f) & 0xFFFFu);
-      named_bar_sync(bar, kXsReducerWarps * 32);
-      const int64_t r0 = static_cast<int64_t>(tile) * kXsRows;
-      const int local_items = p.M * 2;
-      const int items = *(volatile int*)&abort_flag ? local_items : local_items + p.M * 4 * (p.world - 1);
-      for (int q = t; q < items; q += kXsReducerWarps * 32) {
-        if (q < local_items) {
-          const int half = q & 1, mm = q >> 1;
-          if (r0 + half * 8 + 8 > p.N) continue;
-          *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + static_cast<int64_t>(mm) * p.y_sm + p.n_offset +
-                                    r0 + half * 8) = *reinterpret_cast<const uint4*>(tile_out + mm * kXsRows + half * 8);
-        } else {
-          const int qq = q - local_items;
-          const int piece = qq & 3, mm = (qq >> 2) % p.M, k = (qq >> 2) / p.M;
-          if (r0 + piece * 4 + 4 > p.N) continue;
-          const int rr = k < p.rank ? k : k + 1;
-          const uint2 d = *reinterpret_cast<const uint2*>(tile_out + mm * kXsRows + piece * 4);
-          const uint64_t hi = static_cast<uint64_t>(xchg_flag_xs(calls)) << 32;
-          const int64_t col = p.n_offset + r0 + piece * 4;
-          uint8_t* dst = p.xchg_peers[rr] + kGemvXchgCtrlBytes + (calls & 1) * gemv_xchg_slot_bytes(p.n_total) +
-                         mm * 4 * p.n_total + col * 4;
-          asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(hi | d.x), "l"(hi | d.y)
-                       : "memory");
-        }
-      }
-      named_bar_sync(bar, kXsReducerWarps * 32);
-    } else if (m < p.M && n < p.N) {
-      const int64_t off = (n >> 3) * p.y_s8 + static_cast<int64_t>(m) * p.y_sm + (n & 7);
-      if (p.y_bf16) {
-        static_cast<uint16_t*>(p.y)[off] = static_cast<uint16_t>(pack_bf16x2(sum, 0.f) & 0xFFFFu);
-      } else if (p.accumulate) {
-        static_cast<float*>(p.y)[off] += sum;
-      } else {
-        static_cast<float*>(p.y)[off] = sum;
-      }
-    }
   }
 
   if constexpr (GATHER) {
