@@ -704,15 +704,16 @@ cudaError_t launch_moe_gemv(const MoeArgs& a, cudaStream_t stream) {
 // double-buffered shared array handed over with mbarriers; the reducers sum
 // them in warp order, apply SwiGLU and store h in bf16.
 constexpr int kGuWarps = 16;
-constexpr int kGuThreads = (kGuWarps + 1) * 32;
+constexpr int kGuWarpProducer = kGuWarps, kGuWarpReducer = kGuWarps + 1;
+constexpr int kGuThreads = (kGuWarps + 2) * 32;  // + the producer and the reducer warp
 constexpr int kGuMaxStages = 8;
-constexpr int kGuReducerWarps = 4;
-constexpr int kGuReducerSets = kGuWarps / kGuReducerWarps;
 constexpr int kGuHeader = 1024;
 constexpr int kGuRedBytes = 2 * kGuWarps * 32 * 32;  // 2 buffers x 16 warps x 32 lanes x (gate, up) float4
 
 template <int FMT, int GPW>
-__global__ void __launch_bounds__(kGuThreads, 1) moe_gateup_xs(const MoeArgs a, int stages, int pair_pitch) {
+// 18 warps spread 5 + 5 + 4 + 4 over the sub-partitions: 96 registers per
+// thread is the most that launches.
+__global__ void __maxnreg__(96) moe_gateup_xs(const MoeArgs a, int stages, int pair_pitch) {
   using F = GemvFmt<FMT>;
   constexpr int kSteps = F::kSteps;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -737,7 +738,7 @@ __global__ void __launch_bounds__(kGuThreads, 1) moe_gateup_xs(const MoeArgs a, 
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&red_full[b], kGuWarps * 32);
-      mbar_init(&red_empty[b], kGuReducerWarps * 32);
+      mbar_init(&red_empty[b], 32);
     }
     abort_flag = 0;
     fence_mbar_init();
@@ -752,7 +753,7 @@ __global__ void __launch_bounds__(kGuThreads, 1) moe_gateup_xs(const MoeArgs a, 
   const int64_t items = static_cast<int64_t>(hdr[0]) * tiles;
   const int64_t i_begin = blockIdx.x * items / gridDim.x, i_end = (blockIdx.x + 1) * items / gridDim.x;
 
-  if (warp == kGuWarps) {
+  if (warp == kGuWarpProducer) {
     // ---------------------------------------------------------- producer --
     const uint64_t pol = l2_evict_first_policy();
     uint32_t it = 0;
@@ -792,30 +793,75 @@ __global__ void __launch_bounds__(kGuThreads, 1) moe_gateup_xs(const MoeArgs a, 
     return;
   }
 
+  if (warp == kGuWarpReducer) {
+    // ---------------------------------------------------------- reducer --
+    // Lane l sums the 16 warps' (gate, up) float4 partials of fragment lane
+    // l in warp order: item rows (MMA rows l / 4, + 8) x problem vectors
+    // 2 (l % 4), + 1; h = silu(gate) * up in bf16.
+    uint16_t* h = reinterpret_cast<uint16_t*>(a.ws + a.L.h);
+    const int m0 = 2 * (lane & 3);
+    int staged = -1, nx = 0, pair0 = 0, pair1 = 0;
+    int local = 0;
+    for (int64_t i = i_begin; i < i_end; ++i, ++local) {
+      const int pidx = static_cast<int>(i / tiles);
+      const int tile = static_cast<int>(i % tiles);
+      if (pidx != staged) {
+        const MoeProblem pr = probs[pidx];
+        nx = pr.nx;
+        pair0 = m0 < nx ? pairs[pr.first + m0] : 0;
+        pair1 = m0 + 1 < nx ? pairs[pr.first + m0 + 1] : 0;
+        staged = pidx;
+      }
+      const int rbuf = local & 1;
+      if (!mbar_try_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u) && !*(volatile int*)&abort_flag) {
+        if (!mbar_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u)) abort_flag = 1;
+      }
+      const float4* rp = red + (rbuf * kGuWarps * 32 + lane) * 2;
+      float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int w = 0; w < kGuWarps; ++w) {
+        const float4 gv = rp[w * 64], uv = rp[w * 64 + 1];
+        g.x += gv.x;
+        g.y += gv.y;
+        g.z += gv.z;
+        g.w += gv.w;
+        u.x += uv.x;
+        u.y += uv.y;
+        u.z += uv.z;
+        u.w += uv.w;
+      }
+      mbar_arrive(&red_empty[rbuf]);
+      if (*(volatile int*)&abort_flag) continue;
+      const float gs[4] = {g.x, g.y, g.z, g.w}, us[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int m = m0 + (j & 1);
+        if (m >= nx) continue;
+        const int rowp = (lane >> 2) + 8 * (j >> 1);                 // MMA row
+        const int row = rowp < 8 ? 2 * rowp : 2 * (rowp - 8) + 1;  // weight row of the tile
+        h[static_cast<int64_t>((j & 1) ? pair1 : pair0) * a.I + tile * kTileRows + row] =
+            static_cast<uint16_t>(pack_bf16x2(silu(gs[j]) * us[j], 0.f) & 0xFFFFu);
+      }
+    }
+    return;
+  }
+
   // ------------------------------------------------------------ consumers --
   const int r = lane >> 2, c = lane & 3;
   const bool ftz = a.ftz != 0;
-  const int red_set = warp / kGuReducerWarps;
   const uint8_t* ra0 = stg + r * pair_pitch + warp * GPW * F::kGroupBytes;
   uint2 Bx[GPW][kSteps];
   int staged = -1;
   MoeProblem pr{};
-  int stage = 0, red_turn = 0;
+  int stage = 0;
   uint32_t phase = 0u;
   int local = 0;
-  // the reducer thread's output column (the same in every item)
-  const int t_red = (warp % kGuReducerWarps) * 32 + lane;
-  const int l_red = t_red >> 2, j_red = t_red & 3;
-  const int m_red = 2 * (l_red & 3) + (j_red & 1);
-  int pair_red = 0;
   for (int64_t i = i_begin; i < i_end; ++i, ++local) {
     const int pidx = static_cast<int>(i / tiles);
-    const int tile = static_cast<int>(i % tiles);
     if (pidx != staged) {
       // every warp has its fragments of the previous problem
       named_bar_sync(1, kGuWarps * 32);
       pr = probs[pidx];
-      pair_red = m_red < pr.nx ? pairs[pr.first + m_red] : 0;
       // the problem's activation rows (nx <= 8), 16-byte pieces
       const int pieces = a.H / 8;
       for (int q = threadIdx.x; q < pr.nx * pieces; q += kGuWarps * 32) {
@@ -860,7 +906,7 @@ __global__ void __launch_bounds__(kGuThreads, 1) moe_gateup_xs(const MoeArgs a, 
       phase ^= 1u;
     }
 
-    // hand the partials to this item's reducers
+    // hand the partials to the reducer warp
     const int rbuf = local & 1;
     if (local >= 2 && !mbar_try_wait(&red_empty[rbuf], static_cast<uint32_t>((local >> 1) - 1) & 1u) &&
         !*(volatile int*)&abort_flag) {
@@ -870,29 +916,6 @@ __global__ void __launch_bounds__(kGuThreads, 1) moe_gateup_xs(const MoeArgs a, 
     my[0] = make_float4(accg[0], accg[1], accg[2], accg[3]);
     my[1] = make_float4(accu[0], accu[1], accu[2], accu[3]);
     mbar_arrive(&red_full[rbuf]);
-    const bool mine = red_turn == red_set;
-    if (++red_turn == kGuReducerSets) red_turn = 0;
-    if (!mine) continue;
-
-    // ---------------------------------------------------- reduction ----
-    if (!mbar_try_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u) && !*(volatile int*)&abort_flag) {
-      if (!mbar_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u)) abort_flag = 1;
-    }
-    const float* rp = reinterpret_cast<const float*>(red + (rbuf * kGuWarps * 32 + l_red) * 2) + j_red;
-    float gsum = 0.f, usum = 0.f;
-#pragma unroll
-    for (int w = 0; w < kGuWarps; ++w) {
-      gsum += rp[w * 32 * 8];
-      usum += rp[w * 32 * 8 + 4];
-    }
-    mbar_arrive(&red_empty[rbuf]);
-    const int rowp = (l_red >> 2) + 8 * (j_red >> 1);      // MMA row
-    const int row = rowp < 8 ? 2 * rowp : 2 * (rowp - 8) + 1;  // weight row of the tile
-    if (ready && m_red < pr.nx) {
-      uint16_t* h = reinterpret_cast<uint16_t*>(a.ws + a.L.h);
-      h[static_cast<int64_t>(pair_red) * a.I + tile * kTileRows + row] =
-          static_cast<uint16_t>(pack_bf16x2(silu(gsum) * usum, 0.f) & 0xFFFFu);
-    }
   }
 }
 
@@ -949,16 +972,17 @@ cudaError_t launch_moe_gateup_xs(const MoeArgs& a, cudaStream_t stream, bool* la
 // store w_{t,j} * y into the per-pair outputs.
 constexpr int kDnGroups = 6;
 constexpr int kDnWarps = 12;
-constexpr int kDnThreads = (kDnWarps + 1) * 32;
+constexpr int kDnWarpProducer = kDnWarps, kDnWarpReducer = kDnWarps + 1;
+constexpr int kDnThreads = (kDnWarps + 2) * 32;  // + the producer and the reducer warp
 constexpr int kDnMaxStages = 12;
-constexpr int kDnReducerWarps = 4;
-constexpr int kDnReducerSets = kDnWarps / kDnReducerWarps;
 constexpr int kDnItemRows = 64;
 constexpr int kDnHeader = 1024;
 constexpr int kDnRedBytes = 2 * kDnWarps * 32 * 32;  // 2 buffers x 12 warps x 32 lanes x 2 float4
 
 template <int FMT>
-__global__ void __launch_bounds__(kDnThreads, 1) moe_down_xs(const MoeArgs a, int stages, int pair_pitch) {
+// 14 warps spread 4 + 4 + 3 + 3 over the sub-partitions: 120 registers per
+// thread still launches.
+__global__ void __maxnreg__(120) moe_down_xs(const MoeArgs a, int stages, int pair_pitch) {
   using F = GemvFmt<FMT>;
   constexpr int kSteps = F::kSteps;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -982,7 +1006,7 @@ __global__ void __launch_bounds__(kDnThreads, 1) moe_down_xs(const MoeArgs a, in
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&red_full[b], kDnWarps * 32);
-      mbar_init(&red_empty[b], kDnReducerWarps * 32);
+      mbar_init(&red_empty[b], 32);
     }
     abort_flag = 0;
     fence_mbar_init();
@@ -998,7 +1022,7 @@ __global__ void __launch_bounds__(kDnThreads, 1) moe_down_xs(const MoeArgs a, in
   const int64_t items = static_cast<int64_t>(hdr[0]) * tiles;
   const int64_t i_begin = blockIdx.x * items / gridDim.x, i_end = (blockIdx.x + 1) * items / gridDim.x;
 
-  if (warp == kDnWarps) {
+  if (warp == kDnWarpProducer) {
     // ---------------------------------------------------------- producer --
     const uint64_t pol = l2_evict_first_policy();
     uint32_t it = 0;
@@ -1033,32 +1057,85 @@ __global__ void __launch_bounds__(kDnThreads, 1) moe_down_xs(const MoeArgs a, in
     return;
   }
 
+  if (warp == kDnWarpReducer) {
+    // ---------------------------------------------------------- reducer --
+    // Lane l sums, for each of the item's 4 row blocks b, the 6 group
+    // partials (warps 6 (b / 2) + g, accumulator b % 2) of fragment lane l in
+    // group order, and stores w_{t,j} * y into the per-pair outputs: rows of
+    // MMA rows l / 4, + 8 of block b, problem vectors 2 (l % 4), + 1.
+    float* part = reinterpret_cast<float*>(a.ws + a.L.part);
+    const int m0 = 2 * (lane & 3);
+    int staged = -1, nx = 0, pair0 = 0, pair1 = 0;
+    float wt0 = 0.f, wt1 = 0.f;
+    int local = 0;
+    for (int64_t i = i_begin; i < i_end; ++i, ++local) {
+      const int pidx = static_cast<int>(i / tiles);
+      const int tile = static_cast<int>(i % tiles);
+      if (pidx != staged) {
+        const MoeProblem pr = probs[pidx];
+        nx = pr.nx;
+        pair0 = m0 < nx ? pairs[pr.first + m0] : 0;
+        pair1 = m0 + 1 < nx ? pairs[pr.first + m0 + 1] : 0;
+        wt0 = m0 < nx ? a.wts[pair0] : 0.f;
+        wt1 = m0 + 1 < nx ? a.wts[pair1] : 0.f;
+        staged = pidx;
+      }
+      const int rbuf = local & 1;
+      if (!mbar_try_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u) && !*(volatile int*)&abort_flag) {
+        if (!mbar_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u)) abort_flag = 1;
+      }
+      float4 v[4];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const float4* rp = red + ((rbuf * kDnWarps + (b >> 1) * kDnGroups) * 32 + lane) * 2 + (b & 1);
+        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int gg = 0; gg < kDnGroups; ++gg) {
+          const float4 q = rp[gg * 64];
+          sum.x += q.x;
+          sum.y += q.y;
+          sum.z += q.z;
+          sum.w += q.w;
+        }
+        v[b] = sum;
+      }
+      mbar_arrive(&red_empty[rbuf]);
+      if (*(volatile int*)&abort_flag) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int m = m0 + (j & 1);
+        if (m >= nx) continue;
+        const int rowp = (lane >> 2) + 8 * (j >> 1);
+        const int row16 = rowp < 8 ? 2 * rowp : 2 * (rowp - 8) + 1;
+        const float wt = (j & 1) ? wt1 : wt0;
+        float* dst = part + static_cast<int64_t>((j & 1) ? pair1 : pair0) * a.H + tile * kDnItemRows + row16;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const float val = j == 0 ? v[b].x : j == 1 ? v[b].y : j == 2 ? v[b].z : v[b].w;
+          dst[16 * b] = wt * val;
+        }
+      }
+    }
+    return;
+  }
+
   // ------------------------------------------------------------ consumers --
   const int r = lane >> 2, c = lane & 3;
   const bool ftz = a.ftz != 0;
   const int g = warp % kDnGroups, rbp = warp / kDnGroups;  // decode group, row-block pair
-  const int red_set = warp / kDnReducerWarps;
   // MMA row r of row block b = pair 8b + r (weight rows 16b + 2r, +1)
   const uint8_t* ra0 = stg + (16 * rbp + r) * pair_pitch + g * F::kGroupBytes;
   uint2 Bx[kSteps];
   int staged = -1;
   MoeProblem pr{};
-  int stage = 0, red_turn = 0;
+  int stage = 0;
   uint32_t phase = 0u;
   int local = 0;
-  const int t_red = (warp % kDnReducerWarps) * 32 + lane;
-  const int l_red = t_red >> 2, j_red = t_red & 3;
-  const int m_red = 2 * (l_red & 3) + (j_red & 1);
-  int pair_red = 0;
-  float wt_red = 0.f;
   for (int64_t i = i_begin; i < i_end; ++i, ++local) {
     const int pidx = static_cast<int>(i / tiles);
-    const int tile = static_cast<int>(i % tiles);
     if (pidx != staged) {
       named_bar_sync(1, kDnWarps * 32);
       pr = probs[pidx];
-      pair_red = m_red < pr.nx ? pairs[pr.first + m_red] : 0;
-      wt_red = m_red < pr.nx ? a.wts[pair_red] : 0.f;
       const int pieces = a.I / 8;
       for (int q = threadIdx.x; q < pr.nx * pieces; q += kDnWarps * 32) {
         const int m = q / pieces, pc = q - m * pieces;
@@ -1094,6 +1171,7 @@ __global__ void __launch_bounds__(kDnThreads, 1) moe_down_xs(const MoeArgs a, in
       phase ^= 1u;
     }
 
+    // hand the partials to the reducer warp
     const int rbuf = local & 1;
     if (local >= 2 && !mbar_try_wait(&red_empty[rbuf], static_cast<uint32_t>((local >> 1) - 1) & 1u) &&
         !*(volatile int*)&abort_flag) {
@@ -1103,34 +1181,6 @@ __global__ void __launch_bounds__(kDnThreads, 1) moe_down_xs(const MoeArgs a, in
     my[0] = make_float4(acc0[0], acc0[1], acc0[2], acc0[3]);
     my[1] = make_float4(acc1[0], acc1[1], acc1[2], acc1[3]);
     mbar_arrive(&red_full[rbuf]);
-    const bool mine = red_turn == red_set;
-    if (++red_turn == kDnReducerSets) red_turn = 0;
-    if (!mine) continue;
-
-    // ---------------------------------------------------- reduction ----
-    if (!mbar_try_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u) && !*(volatile int*)&abort_flag) {
-      if (!mbar_wait(&red_full[rbuf], static_cast<uint32_t>(local >> 1) & 1u)) abort_flag = 1;
-    }
-    float v[4];
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {  // row block b of the item: warps (b / 2) * 6 + g, accumulator b % 2
-      const float* rp = reinterpret_cast<const float*>(red + ((rbuf * kDnWarps + (b >> 1) * kDnGroups) * 32 + l_red) * 2 +
-                                                       (b & 1)) +
-                        j_red;
-      float sum = 0.f;
-#pragma unroll
-      for (int gg = 0; gg < kDnGroups; ++gg) sum += rp[gg * 32 * 8];
-      v[b] = sum;
-    }
-    mbar_arrive(&red_empty[rbuf]);
-    if (ready && m_red < pr.nx) {
-      const int rowp = (l_red >> 2) + 8 * (j_red >> 1);
-      const int row16 = rowp < 8 ? 2 * rowp : 2 * (rowp - 8) + 1;
-      float* part = reinterpret_cast<float*>(a.ws + a.L.part) + static_cast<int64_t>(pair_red) * a.H +
-                    tile * kDnItemRows + row16;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) part[16 * b] = wt_red * v[b];
-    }
   }
 }
 
