@@ -108,7 +108,28 @@ struct MoeArgs {
   int T, topk, H, I, e0, E_local;
   uint8_t* ws;
   MoeLayout L;
+  // Few pairs (T * topk <= kMoeDirectPairs): no routing kernel; pair p is
+  // problem p (expert ids[p], one row), the pair list the identity.
+  int direct;
 };
+
+constexpr int kMoeDirectPairs = 16;
+
+// Problem pidx, pair-list entry idx and the problem count, routed or direct.
+__device__ __forceinline__ MoeProblem moe_problem(const MoeArgs& a, const MoeProblem* probs, int pidx) {
+  if (a.direct) {
+    const int e = a.ids[pidx] - a.e0;
+    const bool local = e >= 0 && e < a.E_local;
+    return MoeProblem{local ? e : 0, pidx, local ? 1 : 0, 0};
+  }
+  return probs[pidx];
+}
+__device__ __forceinline__ int moe_pair(const MoeArgs& a, const int* pairs, int idx) {
+  return a.direct ? idx : pairs[idx];
+}
+__device__ __forceinline__ int moe_problem_count(const MoeArgs& a, const int* hdr) {
+  return a.direct ? a.T * a.topk : hdr[0];
+}
 
 // ------------------------------------------------------------- routing ----
 
@@ -316,7 +337,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
   const int* hdr = reinterpret_cast<const int*>(a.ws + a.L.hdr);
   const int* pairs = reinterpret_cast<const int*>(a.ws + a.L.pairs);
   const MoeProblem* probs = reinterpret_cast<const MoeProblem*>(a.ws + a.L.problems);
-  const int64_t items = static_cast<int64_t>(hdr[0]) * tiles;
+  const int64_t items = static_cast<int64_t>(moe_problem_count(a, hdr)) * tiles;
   const int64_t i_begin = blockIdx.x * items / gridDim.x, i_end = (blockIdx.x + 1) * items / gridDim.x;
 
   if (warp == kMoeConsumers) {
@@ -329,7 +350,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     const uint32_t bytes = static_cast<uint32_t>(rb);
     uint32_t it = 0;
     for (int64_t i = i_begin; i < i_end; ++i, ++it) {
-      const MoeProblem pr = probs[i / tiles];
+      const MoeProblem pr = moe_problem(a, probs, static_cast<int>(i / tiles));
       const int tile = static_cast<int>(i % tiles);
       const int s = static_cast<int>(it % stages);
       int go = 0;
@@ -383,15 +404,15 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     const int pidx = static_cast<int>(i / tiles);
     const int tile = static_cast<int>(i % tiles);
     if (pidx != staged) {
-      pr = probs[pidx];
-      my_pair = my_m < pr.nx ? pairs[pr.first + my_m] : 0;
+      pr = moe_problem(a, probs, pidx);
+      my_pair = my_m < pr.nx ? moe_pair(a, pairs, pr.first + my_m) : 0;
       if constexpr (PHASE == 2) my_wt = my_m < pr.nx ? a.wts[my_pair] : 0.f;
       if constexpr (PHASE == 1) {
-        auto src = [&](int m) { return a.x + static_cast<int64_t>(pairs[pr.first + m] / a.topk) * a.x_stride; };
+        auto src = [&](int m) { return a.x + static_cast<int64_t>(moe_pair(a, pairs, pr.first + m) / a.topk) * a.x_stride; };
         moe_stage_rows<FMT>(pr.nx, K, src, xs, x_pitch, reinterpret_cast<uint8_t*>(gred), gt, bar_id);
       } else {
         const uint16_t* h = reinterpret_cast<const uint16_t*>(a.ws + a.L.h);
-        auto src = [&](int m) { return h + static_cast<int64_t>(pairs[pr.first + m]) * a.I; };
+        auto src = [&](int m) { return h + static_cast<int64_t>(moe_pair(a, pairs, pr.first + m)) * a.I; };
         moe_stage_rows<FMT>(pr.nx, K, src, xs, x_pitch, reinterpret_cast<uint8_t*>(gred), gt, bar_id);
       }
       staged = pidx;
@@ -750,7 +771,7 @@ __global__ void __maxnreg__(96) moe_gateup_xs(const MoeArgs a, int stages, int p
   const int* hdr = reinterpret_cast<const int*>(a.ws + a.L.hdr);
   const int* pairs = reinterpret_cast<const int*>(a.ws + a.L.pairs);
   const MoeProblem* probs = reinterpret_cast<const MoeProblem*>(a.ws + a.L.problems);
-  const int64_t items = static_cast<int64_t>(hdr[0]) * tiles;
+  const int64_t items = static_cast<int64_t>(moe_problem_count(a, hdr)) * tiles;
   const int64_t i_begin = blockIdx.x * items / gridDim.x, i_end = (blockIdx.x + 1) * items / gridDim.x;
 
   if (warp == kGuWarpProducer) {
@@ -760,7 +781,7 @@ __global__ void __maxnreg__(96) moe_gateup_xs(const MoeArgs a, int stages, int p
     int stage = 0;
     uint32_t phase = 0u;
     for (int64_t i = i_begin; i < i_end; ++i, ++it) {
-      const MoeProblem pr = probs[i / tiles];
+      const MoeProblem pr = moe_problem(a, probs, static_cast<int>(i / tiles));
       const int tile = static_cast<int>(i % tiles);
       int go = 0;
       if (lane == 0) {
@@ -806,10 +827,10 @@ __global__ void __maxnreg__(96) moe_gateup_xs(const MoeArgs a, int stages, int p
       const int pidx = static_cast<int>(i / tiles);
       const int tile = static_cast<int>(i % tiles);
       if (pidx != staged) {
-        const MoeProblem pr = probs[pidx];
+        const MoeProblem pr = moe_problem(a, probs, pidx);
         nx = pr.nx;
-        pair0 = m0 < nx ? pairs[pr.first + m0] : 0;
-        pair1 = m0 + 1 < nx ? pairs[pr.first + m0 + 1] : 0;
+        pair0 = m0 < nx ? moe_pair(a, pairs, pr.first + m0) : 0;
+        pair1 = m0 + 1 < nx ? moe_pair(a, pairs, pr.first + m0 + 1) : 0;
         staged = pidx;
       }
       const int rbuf = local & 1;
@@ -861,12 +882,12 @@ __global__ void __maxnreg__(96) moe_gateup_xs(const MoeArgs a, int stages, int p
     if (pidx != staged) {
       // every warp has its fragments of the previous problem
       named_bar_sync(1, kGuWarps * 32);
-      pr = probs[pidx];
+      pr = moe_problem(a, probs, pidx);
       // the problem's activation rows (nx <= 8), 16-byte pieces
       const int pieces = a.H / 8;
       for (int q = threadIdx.x; q < pr.nx * pieces; q += kGuWarps * 32) {
         const int m = q / pieces, pc = q - m * pieces;
-        const int tok = pairs[pr.first + m] / a.topk;
+        const int tok = moe_pair(a, pairs, pr.first + m) / a.topk;
         reinterpret_cast<uint4*>(xbuf + m * a.H * 2)[pc] =
             __ldg(reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(tok) * a.x_stride) + pc);
       }
@@ -1019,7 +1040,7 @@ __global__ void __maxnreg__(120) moe_down_xs(const MoeArgs a, int stages, int pa
   const int* pairs = reinterpret_cast<const int*>(a.ws + a.L.pairs);
   const MoeProblem* probs = reinterpret_cast<const MoeProblem*>(a.ws + a.L.problems);
   const uint16_t* hbuf = reinterpret_cast<const uint16_t*>(a.ws + a.L.h);
-  const int64_t items = static_cast<int64_t>(hdr[0]) * tiles;
+  const int64_t items = static_cast<int64_t>(moe_problem_count(a, hdr)) * tiles;
   const int64_t i_begin = blockIdx.x * items / gridDim.x, i_end = (blockIdx.x + 1) * items / gridDim.x;
 
   if (warp == kDnWarpProducer) {
@@ -1029,7 +1050,7 @@ __global__ void __maxnreg__(120) moe_down_xs(const MoeArgs a, int stages, int pa
     int stage = 0;
     uint32_t phase = 0u;
     for (int64_t i = i_begin; i < i_end; ++i, ++it) {
-      const MoeProblem pr = probs[i / tiles];
+      const MoeProblem pr = moe_problem(a, probs, static_cast<int>(i / tiles));
       const int tile = static_cast<int>(i % tiles);
       int go = 0;
       if (lane == 0) {
@@ -1072,10 +1093,10 @@ __global__ void __maxnreg__(120) moe_down_xs(const MoeArgs a, int stages, int pa
       const int pidx = static_cast<int>(i / tiles);
       const int tile = static_cast<int>(i % tiles);
       if (pidx != staged) {
-        const MoeProblem pr = probs[pidx];
+        const MoeProblem pr = moe_problem(a, probs, pidx);
         nx = pr.nx;
-        pair0 = m0 < nx ? pairs[pr.first + m0] : 0;
-        pair1 = m0 + 1 < nx ? pairs[pr.first + m0 + 1] : 0;
+        pair0 = m0 < nx ? moe_pair(a, pairs, pr.first + m0) : 0;
+        pair1 = m0 + 1 < nx ? moe_pair(a, pairs, pr.first + m0 + 1) : 0;
         wt0 = m0 < nx ? a.wts[pair0] : 0.f;
         wt1 = m0 + 1 < nx ? a.wts[pair1] : 0.f;
         staged = pidx;
@@ -1135,12 +1156,12 @@ __global__ void __maxnreg__(120) moe_down_xs(const MoeArgs a, int stages, int pa
     const int pidx = static_cast<int>(i / tiles);
     if (pidx != staged) {
       named_bar_sync(1, kDnWarps * 32);
-      pr = probs[pidx];
+      pr = moe_problem(a, probs, pidx);
       const int pieces = a.I / 8;
       for (int q = threadIdx.x; q < pr.nx * pieces; q += kDnWarps * 32) {
         const int m = q / pieces, pc = q - m * pieces;
         reinterpret_cast<uint4*>(xbuf + m * a.I * 2)[pc] =
-            __ldg(reinterpret_cast<const uint4*>(hbuf + static_cast<int64_t>(pairs[pr.first + m]) * a.I) + pc);
+            __ldg(reinterpret_cast<const uint4*>(hbuf + static_cast<int64_t>(moe_pair(a, pairs, pr.first + m)) * a.I) + pc);
       }
       named_bar_sync(1, kDnWarps * 32);
 #pragma unroll
@@ -1215,9 +1236,15 @@ cudaError_t launch_moe_down_xs(const MoeArgs& a, cudaStream_t stream, bool* laun
 }
 
 template <int FMT>
-cudaError_t moe_run(const MoeArgs& a, cudaStream_t stream, const MoeEp* ep = nullptr) {
-  MoeArgs args = a;
-  {
+cudaError_t moe_run(const MoeArgs& a0, cudaStream_t stream, const MoeEp* ep = nullptr) {
+  MoeArgs args = a0;
+  // A few pairs: each is its own problem and the routing kernel (a launch
+  // and a dependent step in front of the weight stream) is skipped; it
+  // costs a second read of an expert's weights only when two of the pairs
+  // pick the same expert.
+  args.direct = ep == nullptr && static_cast<int64_t>(a0.T) * a0.topk <= kMoeDirectPairs;
+  const MoeArgs& a = args;
+  if (!a.direct) {
     void* kargs[] = {&args};
     const size_t smem = size_t(3) * a.E_local * sizeof(int);
     cudaError_t e = launch_pdl(reinterpret_cast<const void*>(moe_route), dim3(1), dim3(kRouteThreads), smem, stream,

@@ -97,3 +97,31 @@ def test_moe_expert_parallel_partials_sum_to_full(cuda):
         assert ok, rel
     ok, rel = tolerance_ok(parts[0] + parts[1], full, bf16_out=False)
     assert ok, rel
+
+
+@pytest.mark.parametrize("fid", [F.Q4_0, F.Q8_0], ids=lambda f: F.NAMES[f])
+@pytest.mark.parametrize("e0", [0, 4])
+def test_moe_few_pairs_repeated_and_foreign_experts(cuda, fid, e0):
+    """T * topk <= 16 pairs (each pair its own problem, no routing kernel):
+    an expert picked twice by one token and by both tokens, ids outside the
+    local range (skipped), a local range that starts past expert 0, and a
+    token with no local expert (its output is the empty sum); bitwise
+    repeatable."""
+    E, H, I, T, topk = 12, 2048, 768, 2, 8
+    wg, wu, wd, x, _, w = _case(fid, E, H, I, T, topk, seed=61)
+    ids = np.array([[5, 5, 7, 9, 4, 11, 6, 8],
+                    [7, -1, 15, 5, 9, 100, 10, 4]], dtype=np.int32)
+    if e0:
+        ids[1] = [0, 1, 2, 3, -1, 20, 1, 0]  # no expert of [e0, e0 + E_local)
+    E_local = E - e0
+    gu, dd = I * F.row_bytes(fid, H), H * F.row_bytes(fid, I)
+    wgl, wul, wdl = wg[e0 * gu:], wu[e0 * gu:], wd[e0 * dd:]
+    y = _run(fid, wgl, wul, wdl, x, ids, w, H, I, E_local, e0=e0).cpu().numpy()
+    ref = oracle.moe_ffn_f64(fid, wgl, wul, wdl, x, ids, w, H, I, E_local, expert_first=e0)
+    ok, rel = tolerance_ok(y, ref, bf16_out=False)
+    assert ok, rel
+    if e0:
+        assert not y[1].any()
+    y2 = _run(fid, wgl, wul, wdl, x, ids, w, H, I, E_local, e0=e0).cpu().numpy()
+    assert np.array_equal(y, y2)
+    assert sp.device_status() == 0
