@@ -80,6 +80,66 @@ __device__ __forceinline__ float byte_as_f32_magic(uint32_t w) {
   return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | I));
 }
 
+// ------------------------------------------------ exact fp16-route decode --
+// Two quants placed in the mantissas of an fp16 pair by one LOP3
+// (u = 2^e + q), then u * d + c per weight by a mixed-precision FMA with the
+// fp16 scale d itself: u * d is exact inside the FMA and c = -(2^e + bias) d
+// and the result (q - bias) d have at most 19 significant bits, so nothing
+// rounds before the final bf16 conversion.
+// (a & m) | o and (a & m) ^ o in one LOP3 each.
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t o) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(m), "r"(o));
+  return r;
+}
+__device__ __forceinline__ uint32_t lop_and_xor(uint32_t a, uint32_t m, uint32_t o) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(a), "r"(m), "r"(o));
+  return r;
+}
+// u.lo * d + c and u.hi * d + c for the fp16 pair u and the fp16 scale d,
+// in fp32 with one rounding.
+__device__ __forceinline__ float fmah_lo(uint32_t u, unsigned short d, float c) {
+  float r;
+  asm("{ .reg .b16 l, h; mov.b32 {l, h}, %1; fma.rn.f32.f16 %0, l, %2, %3; }" : "=f"(r) : "r"(u), "h"(d), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float fmah_hi(uint32_t u, unsigned short d, float c) {
+  float r;
+  asm("{ .reg .b16 l, h; mov.b32 {l, h}, %1; fma.rn.f32.f16 %0, h, %2, %3; }" : "=f"(r) : "r"(u), "h"(d), "f"(c));
+  return r;
+}
+// The fp16 scale operand: a subnormal scale becomes +0 under ftz, zeros keep
+// their sign, as fp16_bits_to_f32 does.
+__device__ __forceinline__ unsigned short fp16_scale_bits(uint32_t h, bool ftz) {
+  return (ftz && (h & 0x7c00u) == 0u && (h & 0x03ffu) != 0u) ? static_cast<unsigned short>(0)
+                                                             : static_cast<unsigned short>(h);
+}
+// Two weights of the fp16 route, rounded to one bf16 pair (x in the low half).
+__device__ __forceinline__ uint32_t h2pack_lo(uint32_t ux, uint32_t uy, unsigned short d, float c) {
+  return pack_bf16x2(fmah_lo(ux, d, c), fmah_lo(uy, d, c));
+}
+__device__ __forceinline__ uint32_t h2pack_hi(uint32_t ux, uint32_t uy, unsigned short d, float c) {
+  return pack_bf16x2(fmah_hi(ux, d, c), fmah_hi(uy, d, c));
+}
+
+// The product form for outputs that must match bit for bit, zero signs
+// included (the standalone dequant): t = u - (2^e + bias) per fp16 half
+// (exact: |q - bias| <= 128), then fma(t, d, -0), which is t * d rounded once
+// with the IEEE sign of a zero product (+0 + -0 would lose it; -0 + -0
+// keeps it).
+__device__ __forceinline__ uint32_t hsub2(uint32_t u, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(u), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t h2mul_lo(uint32_t tx, uint32_t ty, unsigned short d) {
+  return pack_bf16x2(fmah_lo(tx, d, -0.0f), fmah_lo(ty, d, -0.0f));
+}
+__device__ __forceinline__ uint32_t h2mul_hi(uint32_t tx, uint32_t ty, unsigned short d) {
+  return pack_bf16x2(fmah_hi(tx, d, -0.0f), fmah_hi(ty, d, -0.0f));
+}
+
 // ----------------------------------------- programmatic dependent launch --
 // A kernel launched with programmatic stream serialization lets its
 // successor be scheduled once every CTA has called launch_dependents, and

@@ -15,36 +15,33 @@ namespace spiral {
 
 // ---- Q4_0 ----------------------------------------------------------------
 // qs8 = the 8 qs bytes [8*(part&1), +8) as two little-endian words; `high`
-// selects the high nibbles (weights 16..31 of the block).
-__device__ __forceinline__ uint4 q4_0_decode8(uint32_t w0, uint32_t w1, bool high, float d) {
+// selects the high nibbles (weights 16..31 of the block).  h: the fp16 scale
+// bits (after any flush).  Each nibble becomes u = 1024 + q in an fp16 half
+// (one LOP3 per two), t = u - 1032 = q - 8 exactly, and t * d is one exact
+// product (zero signs as the reference's (q - 8) * d).
+__device__ __forceinline__ uint4 q4_0_decode8(uint32_t w0, uint32_t w1, bool high, unsigned short h) {
   if (high) {
     w0 >>= 4;
     w1 >>= 4;
   }
-  w0 &= 0x0F0F0F0Fu;
-  w1 &= 0x0F0F0F0Fu;
-  constexpr float kBias = 8388616.0f;  // 2^23 + 8
-  uint4 r;
-  r.x = pack_bf16x2((byte_as_f32_magic<0>(w0) - kBias) * d, (byte_as_f32_magic<1>(w0) - kBias) * d);
-  r.y = pack_bf16x2((byte_as_f32_magic<2>(w0) - kBias) * d, (byte_as_f32_magic<3>(w0) - kBias) * d);
-  r.z = pack_bf16x2((byte_as_f32_magic<0>(w1) - kBias) * d, (byte_as_f32_magic<1>(w1) - kBias) * d);
-  r.w = pack_bf16x2((byte_as_f32_magic<2>(w1) - kBias) * d, (byte_as_f32_magic<3>(w1) - kBias) * d);
-  return r;
+  constexpr uint32_t kB = 0x64086408u;  // 1032, 1032
+  const uint32_t a02 = hsub2(lop_and_or(w0, 0x000F000Fu, 0x64006400u), kB);
+  const uint32_t a13 = hsub2(lop_and_or(w0 >> 8, 0x000F000Fu, 0x64006400u), kB);
+  const uint32_t b02 = hsub2(lop_and_or(w1, 0x000F000Fu, 0x64006400u), kB);
+  const uint32_t b13 = hsub2(lop_and_or(w1 >> 8, 0x000F000Fu, 0x64006400u), kB);
+  return make_uint4(h2mul_lo(a02, a13, h), h2mul_hi(a02, a13, h), h2mul_lo(b02, b13, h), h2mul_hi(b02, b13, h));
 }
 
 // ---- Q8_0 ----------------------------------------------------------------
-// 8 int8 quants as two words.  Bytes are biased to unsigned (x ^ 0x80) so the
-// 2^23 magic conversion applies; subtracting 2^23 + 128 restores q exactly.
-__device__ __forceinline__ uint4 q8_0_decode8(uint32_t w0, uint32_t w1, float d) {
-  w0 ^= 0x80808080u;
-  w1 ^= 0x80808080u;
-  constexpr float kBias = 8388736.0f;  // 2^23 + 128
-  uint4 r;
-  r.x = pack_bf16x2((byte_as_f32_magic<0>(w0) - kBias) * d, (byte_as_f32_magic<1>(w0) - kBias) * d);
-  r.y = pack_bf16x2((byte_as_f32_magic<2>(w0) - kBias) * d, (byte_as_f32_magic<3>(w0) - kBias) * d);
-  r.z = pack_bf16x2((byte_as_f32_magic<0>(w1) - kBias) * d, (byte_as_f32_magic<1>(w1) - kBias) * d);
-  r.w = pack_bf16x2((byte_as_f32_magic<2>(w1) - kBias) * d, (byte_as_f32_magic<3>(w1) - kBias) * d);
-  return r;
+// 8 int8 quants as two words; each byte with its sign bit flipped becomes
+// u = 1024 + (q + 128), t = u - 1152 = q exactly, then t * d.
+__device__ __forceinline__ uint4 q8_0_decode8(uint32_t w0, uint32_t w1, unsigned short h) {
+  constexpr uint32_t kB = 0x64806480u;  // 1152, 1152
+  const uint32_t a02 = hsub2(lop_and_xor(w0, 0x00FF00FFu, 0x64806480u), kB);
+  const uint32_t a13 = hsub2(lop_and_xor(w0 >> 8, 0x00FF00FFu, 0x64806480u), kB);
+  const uint32_t b02 = hsub2(lop_and_xor(w1, 0x00FF00FFu, 0x64806480u), kB);
+  const uint32_t b13 = hsub2(lop_and_xor(w1 >> 8, 0x00FF00FFu, 0x64806480u), kB);
+  return make_uint4(h2mul_lo(a02, a13, h), h2mul_hi(a02, a13, h), h2mul_lo(b02, b13, h), h2mul_hi(b02, b13, h));
 }
 
 // ---- Q6_K ----------------------------------------------------------------
@@ -80,15 +77,15 @@ __device__ __forceinline__ uint4 decode8_generic(const uint8_t* blk, int k8, boo
 
 template <>
 __device__ __forceinline__ uint4 decode8_generic<kQ4_0>(const uint8_t* blk, int k8, bool ftz) {
-  const float d = fp16_bits_to_f32(ld_u16_any(blk), ftz);
+  const unsigned short h = fp16_scale_bits(ld_u16_any(blk), ftz);
   const uint8_t* qs = blk + 2 + 8 * (k8 & 1);
-  return q4_0_decode8(ld_u32_2aligned(qs), ld_u32_2aligned(qs + 4), k8 >= 2, d);
+  return q4_0_decode8(ld_u32_2aligned(qs), ld_u32_2aligned(qs + 4), k8 >= 2, h);
 }
 template <>
 __device__ __forceinline__ uint4 decode8_generic<kQ8_0>(const uint8_t* blk, int k8, bool ftz) {
-  const float d = fp16_bits_to_f32(ld_u16_any(blk), ftz);
+  const unsigned short h = fp16_scale_bits(ld_u16_any(blk), ftz);
   const uint8_t* qs = blk + 2 + 8 * k8;
-  return q8_0_decode8(ld_u32_2aligned(qs), ld_u32_2aligned(qs + 4), d);
+  return q8_0_decode8(ld_u32_2aligned(qs), ld_u32_2aligned(qs + 4), h);
 }
 template <>
 __device__ __forceinline__ uint4 decode8_generic<kQ6_K>(const uint8_t* blk, int k8, bool ftz) {

@@ -76,14 +76,14 @@ __device__ __forceinline__ void dq_unit_store(const uint8_t* buf, int lane, uint
       const int b = oc >> 2, part = oc & 3, g = b >> 3, blk = b & 7;
       if (!valid[g]) continue;
       const uint8_t* p = buf + kBB * b;
-      const float d = fp16_bits_to_f32(lds_u16(p), FTZ);
+      const unsigned short h = fp16_scale_bits(lds_u16(p), FTZ);
       uint4 r;
       if constexpr (FMT == kQ4_0) {
         const uint8_t* qs = p + 2 + 8 * (part & 1);
-        r = q4_0_decode8(lds_u32_a2(qs), lds_u32_a2(qs + 4), part >= 2, d);
+        r = q4_0_decode8(lds_u32_a2(qs), lds_u32_a2(qs + 4), part >= 2, h);
       } else {
         const uint8_t* qs = p + 2 + 8 * part;
-        r = q8_0_decode8(lds_u32_a2(qs), lds_u32_a2(qs + 4), d);
+        r = q8_0_decode8(lds_u32_a2(qs), lds_u32_a2(qs + 4), h);
       }
       *reinterpret_cast<uint4*>(dst + dst_off[g] + 32 * blk + 8 * part) = r;
     }

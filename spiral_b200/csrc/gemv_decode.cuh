@@ -75,42 +75,6 @@ __device__ __forceinline__ uint32_t byte_to_f2(uint32_t w) {
   return __byte_perm(w, 0x3F000000u, 0x7054u | (I << 8));
 }
 
-// (a & m) | o and (a & m) ^ o in one LOP3 each.
-__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t o) {
-  uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(m), "r"(o));
-  return r;
-}
-__device__ __forceinline__ uint32_t lop_and_xor(uint32_t a, uint32_t m, uint32_t o) {
-  uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(a), "r"(m), "r"(o));
-  return r;
-}
-// u.lo * d + c and u.hi * d + c for the fp16 pair u and the fp16 scale d,
-// in fp32 with one rounding.
-__device__ __forceinline__ float fmah_lo(uint32_t u, unsigned short d, float c) {
-  float r;
-  asm("{ .reg .b16 l, h; mov.b32 {l, h}, %1; fma.rn.f32.f16 %0, l, %2, %3; }" : "=f"(r) : "r"(u), "h"(d), "f"(c));
-  return r;
-}
-__device__ __forceinline__ float fmah_hi(uint32_t u, unsigned short d, float c) {
-  float r;
-  asm("{ .reg .b16 l, h; mov.b32 {l, h}, %1; fma.rn.f32.f16 %0, h, %2, %3; }" : "=f"(r) : "r"(u), "h"(d), "f"(c));
-  return r;
-}
-// The fp16 scale operand: a subnormal scale becomes +0 under ftz, as
-// fp16_bits_to_f32 flushes it.
-__device__ __forceinline__ unsigned short fp16_scale_bits(uint32_t h, bool ftz) {
-  return (ftz && (h & 0x7c00u) == 0u) ? static_cast<unsigned short>(0) : static_cast<unsigned short>(h);
-}
-// Two weights of the fp16 route, rounded to one bf16 pair (x in the low half).
-__device__ __forceinline__ uint32_t h2pack_lo(uint32_t ux, uint32_t uy, unsigned short d, float c) {
-  return pack_bf16x2(fmah_lo(ux, d, c), fmah_lo(uy, d, c));
-}
-__device__ __forceinline__ uint32_t h2pack_hi(uint32_t ux, uint32_t uy, unsigned short d, float c) {
-  return pack_bf16x2(fmah_hi(ux, d, c), fmah_hi(uy, d, c));
-}
-
 // --------------------------------------------- per-format group decoders --
 // ra / rb: this lane's two feature rows (r and r + 8) at the group start in
 // the stage (4-byte aligned for Q4_0/Q8_0, 2-byte for Q6_K); c = lane % 4;
