@@ -115,20 +115,34 @@ struct MoeArgs {
 
 constexpr int kMoeDirectPairs = 16;
 
-// Problem pidx, pair-list entry idx and the problem count, routed or direct.
+// Problem pidx, pair-list entry idx and the problem count, routed or direct
+// (a template parameter of the kernels, so the routed kernels carry no
+// direct-mode code).
+template <bool DIRECT>
 __device__ __forceinline__ MoeProblem moe_problem(const MoeArgs& a, const MoeProblem* probs, int pidx) {
-  if (a.direct) {
+  if constexpr (DIRECT) {
     const int e = a.ids[pidx] - a.e0;
     const bool local = e >= 0 && e < a.E_local;
     return MoeProblem{local ? e : 0, pidx, local ? 1 : 0, 0};
+  } else {
+    return probs[pidx];
   }
-  return probs[pidx];
 }
-__device__ __forceinline__ int moe_pair(const MoeArgs& a, const int* pairs, int idx) {
-  return a.direct ? idx : pairs[idx];
+template <bool DIRECT>
+__device__ __forceinline__ int moe_pair(const int* pairs, int idx) {
+  if constexpr (DIRECT) {
+    return idx;
+  } else {
+    return pairs[idx];
+  }
 }
+template <bool DIRECT>
 __device__ __forceinline__ int moe_problem_count(const MoeArgs& a, const int* hdr) {
-  return a.direct ? a.T * a.topk : hdr[0];
+  if constexpr (DIRECT) {
+    return a.T * a.topk;
+  } else {
+    return hdr[0];
+  }
 }
 
 // ------------------------------------------------------------- routing ----
@@ -337,7 +351,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
   const int* hdr = reinterpret_cast<const int*>(a.ws + a.L.hdr);
   const int* pairs = reinterpret_cast<const int*>(a.ws + a.L.pairs);
   const MoeProblem* probs = reinterpret_cast<const MoeProblem*>(a.ws + a.L.problems);
-  const int64_t items = static_cast<int64_t>(moe_problem_count(a, hdr)) * tiles;
+  const int64_t items = static_cast<int64_t>(moe_problem_count<false>(a, hdr)) * tiles;
   const int64_t i_begin = blockIdx.x * items / gridDim.x, i_end = (blockIdx.x + 1) * items / gridDim.x;
 
   if (warp == kMoeConsumers) {
@@ -350,7 +364,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     const uint32_t bytes = static_cast<uint32_t>(rb);
     uint32_t it = 0;
     for (int64_t i = i_begin; i < i_end; ++i, ++it) {
-      const MoeProblem pr = moe_problem(a, probs, static_cast<int>(i / tiles));
+      const MoeProblem pr = moe_problem<false>(a, probs, static_cast<int>(i / tiles));
       const int tile = static_cast<int>(i % tiles);
       const int s = static_cast<int>(it % stages);
       int go = 0;
@@ -404,15 +418,15 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     const int pidx = static_cast<int>(i / tiles);
     const int tile = static_cast<int>(i % tiles);
     if (pidx != staged) {
-      pr = moe_problem(a, probs, pidx);
-      my_pair = my_m < pr.nx ? moe_pair(a, pairs, pr.first + my_m) : 0;
+      pr = moe_problem<false>(a, probs, pidx);
+      my_pair = my_m < pr.nx ? moe_pair<false>(pairs, pr.first + my_m) : 0;
       if constexpr (PHASE == 2) my_wt = my_m < pr.nx ? a.wts[my_pair] : 0.f;
       if constexpr (PHASE == 1) {
-        auto src = [&](int m) { return a.x + static_cast<int64_t>(moe_pair(a, pairs, pr.first + m) / a.topk) * a.x_stride; };
+        auto src = [&](int m) { return a.x + static_cast<int64_t>(moe_pair<false>(pairs, pr.first + m) / a.topk) * a.x_stride; };
         moe_stage_rows<FMT>(pr.nx, K, src, xs, x_pitch, reinterpret_cast<uint8_t*>(gred), gt, bar_id);
       } else {
         const uint16_t* h = reinterpret_cast<const uint16_t*>(a.ws + a.L.h);
-        auto src = [&](int m) { return h + static_cast<int64_t>(moe_pair(a, pairs, pr.first + m)) * a.I; };
+        auto src = [&](int m) { return h + static_cast<int64_t>(moe_pair<false>(pairs, pr.first + m)) * a.I; };
         moe_stage_rows<FMT>(pr.nx, K, src, xs, x_pitch, reinterpret_cast<uint8_t*>(gred), gt, bar_id);
       }
       staged = pidx;
@@ -731,7 +745,7 @@ constexpr int kGuMaxStages = 8;
 constexpr int kGuHeader = 1024;
 constexpr int kGuRedBytes = 2 * kGuWarps * 32 * 32;  // 2 buffers x 16 warps x 32 lanes x (gate, up) float4
 
-template <int FMT, int GPW>
+template <int FMT, int GPW, bool DIRECT>
 // 18 warps spread 5 + 5 + 4 + 4 over the sub-partitions: 96 registers per
 // thread is the most that launches.
 __global__ void __maxnreg__(96) moe_gateup_xs(const MoeArgs a, int stages, int pair_pitch) {
@@ -771,7 +785,7 @@ __global__ void __maxnreg__(96) moe_gateup_xs(const MoeArgs a, int stages, int p
   const int* hdr = reinterpret_cast<const int*>(a.ws + a.L.hdr);
   const int* pairs = reinterpret_cast<const int*>(a.ws + a.L.pairs);
   const MoeProblem* probs = reinterpret_cast<const MoeProblem*>(a.ws + a.L.problems);
-  const int64_t items = static_cast<int64_t>(moe_problem_count(a, hdr)) * tiles;
+  const int64_t items = static_cast<int64_t>(moe_problem_count<DIRECT>(a, hdr)) * tiles;
   const int64_t i_begin = blockIdx.x * items / gridDim.x, i_end = (blockIdx.x + 1) * items / gridDim.x;
 
   if (warp == kGuWarpProducer) {
@@ -781,7 +795,7 @@ __global__ void __maxnreg__(96) moe_gateup_xs(const MoeArgs a, int stages, int p
     int stage = 0;
     uint32_t phase = 0u;
     for (int64_t i = i_begin; i < i_end; ++i, ++it) {
-      const MoeProblem pr = moe_problem(a, probs, static_cast<int>(i / tiles));
+      const MoeProblem pr = moe_problem<DIRECT>(a, probs, static_cast<int>(i / tiles));
       const int tile = static_cast<int>(i % tiles);
       int go = 0;
       if (lane == 0) {
@@ -827,10 +841,10 @@ __global__ void __maxnreg__(96) moe_gateup_xs(const MoeArgs a, int stages, int p
       const int pidx = static_cast<int>(i / tiles);
       const int tile = static_cast<int>(i % tiles);
       if (pidx != staged) {
-        const MoeProblem pr = moe_problem(a, probs, pidx);
+        const MoeProblem pr = moe_problem<DIRECT>(a, probs, pidx);
         nx = pr.nx;
-        pair0 = m0 < nx ? moe_pair(a, pairs, pr.first + m0) : 0;
-        pair1 = m0 + 1 < nx ? moe_pair(a, pairs, pr.first + m0 + 1) : 0;
+        pair0 = m0 < nx ? moe_pair<DIRECT>(pairs, pr.first + m0) : 0;
+        pair1 = m0 + 1 < nx ? moe_pair<DIRECT>(pairs, pr.first + m0 + 1) : 0;
         staged = pidx;
       }
       const int rbuf = local & 1;
@@ -882,12 +896,12 @@ __global__ void __maxnreg__(96) moe_gateup_xs(const MoeArgs a, int stages, int p
     if (pidx != staged) {
       // every warp has its fragments of the previous problem
       named_bar_sync(1, kGuWarps * 32);
-      pr = moe_problem(a, probs, pidx);
+      pr = moe_problem<DIRECT>(a, probs, pidx);
       // the problem's activation rows (nx <= 8), 16-byte pieces
       const int pieces = a.H / 8;
       for (int q = threadIdx.x; q < pr.nx * pieces; q += kGuWarps * 32) {
         const int m = q / pieces, pc = q - m * pieces;
-        const int tok = moe_pair(a, pairs, pr.first + m) / a.topk;
+        const int tok = moe_pair<DIRECT>(pairs, pr.first + m) / a.topk;
         reinterpret_cast<uint4*>(xbuf + m * a.H * 2)[pc] =
             __ldg(reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(tok) * a.x_stride) + pc);
       }
@@ -949,29 +963,38 @@ int moe_gu_gpw(const MoeArgs& a) {
   return 0;
 }
 
+// Whether the activation-stationary gate/up kernel serves this layer.
+bool moe_gateup_xs_ok(const MoeArgs& a) {
+  if (moe_gu_gpw(a) == 0) return false;
+  // dense rows, 16-byte aligned, for the pair copies
+  if (reinterpret_cast<uintptr_t>(a.w_gate) % 16 || reinterpret_cast<uintptr_t>(a.w_up) % 16 || a.rb_h % 16)
+    return false;
+  const size_t fixed = kGuHeader + kGuRedBytes + size_t(8) * a.H * 2;
+  const size_t stage = size_t(16) * (2 * static_cast<size_t>(a.rb_h) + 16);
+  return fixed + 3 * stage <= device_max_smem_optin();
+}
+
 template <int FMT>
 cudaError_t launch_moe_gateup_xs(const MoeArgs& a, cudaStream_t stream, bool* launched) {
   *launched = false;
+  if (!moe_gateup_xs_ok(a)) return cudaSuccess;
   const int gpw = moe_gu_gpw(a);
-  if (gpw == 0) return cudaSuccess;
-  // dense rows, 16-byte aligned, for the pair copies
-  if (reinterpret_cast<uintptr_t>(a.w_gate) % 16 || reinterpret_cast<uintptr_t>(a.w_up) % 16 || a.rb_h % 16)
-    return cudaSuccess;
   const int pair_pitch = 2 * static_cast<int>(a.rb_h) + 16;
   const size_t fixed = kGuHeader + kGuRedBytes + size_t(8) * a.H * 2;
   const size_t avail = device_max_smem_optin();
   const size_t stage = size_t(16) * pair_pitch;
-  if (fixed + 3 * stage > avail) return cudaSuccess;
   const int stages = static_cast<int>(std::min<size_t>(kGuMaxStages, (avail - fixed) / stage));
   const size_t smem = fixed + size_t(stages) * stage;
-  auto* kernel = gpw == 1 ? moe_gateup_xs<FMT, 1> : moe_gateup_xs<FMT, 2>;
+  auto* kernel = a.direct ? (gpw == 1 ? moe_gateup_xs<FMT, 1, true> : moe_gateup_xs<FMT, 2, true>)
+                          : (gpw == 1 ? moe_gateup_xs<FMT, 1, false> : moe_gateup_xs<FMT, 2, false>);
+  const int slot = (gpw - 1) * 2 + (a.direct ? 1 : 0);
   int dev = 0;
   cudaGetDevice(&dev);
-  static std::atomic<bool> configured[64][2];
-  if (!configured[dev & 63][gpw - 1].load(std::memory_order_acquire)) {
+  static std::atomic<bool> configured[64][4];
+  if (!configured[dev & 63][slot].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(avail));
     if (e != cudaSuccess) return e;
-    configured[dev & 63][gpw - 1].store(true, std::memory_order_release);
+    configured[dev & 63][slot].store(true, std::memory_order_release);
   }
   MoeArgs args = a;
   int st = stages, pp = pair_pitch;
@@ -1000,7 +1023,7 @@ constexpr int kDnItemRows = 64;
 constexpr int kDnHeader = 1024;
 constexpr int kDnRedBytes = 2 * kDnWarps * 32 * 32;  // 2 buffers x 12 warps x 32 lanes x 2 float4
 
-template <int FMT>
+template <int FMT, bool DIRECT>
 // 14 warps spread 4 + 4 + 3 + 3 over the sub-partitions: 120 registers per
 // thread still launches.
 __global__ void __maxnreg__(120) moe_down_xs(const MoeArgs a, int stages, int pair_pitch) {
@@ -1040,7 +1063,7 @@ __global__ void __maxnreg__(120) moe_down_xs(const MoeArgs a, int stages, int pa
   const int* pairs = reinterpret_cast<const int*>(a.ws + a.L.pairs);
   const MoeProblem* probs = reinterpret_cast<const MoeProblem*>(a.ws + a.L.problems);
   const uint16_t* hbuf = reinterpret_cast<const uint16_t*>(a.ws + a.L.h);
-  const int64_t items = static_cast<int64_t>(moe_problem_count(a, hdr)) * tiles;
+  const int64_t items = static_cast<int64_t>(moe_problem_count<DIRECT>(a, hdr)) * tiles;
   const int64_t i_begin = blockIdx.x * items / gridDim.x, i_end = (blockIdx.x + 1) * items / gridDim.x;
 
   if (warp == kDnWarpProducer) {
@@ -1050,7 +1073,7 @@ __global__ void __maxnreg__(120) moe_down_xs(const MoeArgs a, int stages, int pa
     int stage = 0;
     uint32_t phase = 0u;
     for (int64_t i = i_begin; i < i_end; ++i, ++it) {
-      const MoeProblem pr = moe_problem(a, probs, static_cast<int>(i / tiles));
+      const MoeProblem pr = moe_problem<DIRECT>(a, probs, static_cast<int>(i / tiles));
       const int tile = static_cast<int>(i % tiles);
       int go = 0;
       if (lane == 0) {
@@ -1093,10 +1116,10 @@ __global__ void __maxnreg__(120) moe_down_xs(const MoeArgs a, int stages, int pa
       const int pidx = static_cast<int>(i / tiles);
       const int tile = static_cast<int>(i % tiles);
       if (pidx != staged) {
-        const MoeProblem pr = moe_problem(a, probs, pidx);
+        const MoeProblem pr = moe_problem<DIRECT>(a, probs, pidx);
         nx = pr.nx;
-        pair0 = m0 < nx ? moe_pair(a, pairs, pr.first + m0) : 0;
-        pair1 = m0 + 1 < nx ? moe_pair(a, pairs, pr.first + m0 + 1) : 0;
+        pair0 = m0 < nx ? moe_pair<DIRECT>(pairs, pr.first + m0) : 0;
+        pair1 = m0 + 1 < nx ? moe_pair<DIRECT>(pairs, pr.first + m0 + 1) : 0;
         wt0 = m0 < nx ? a.wts[pair0] : 0.f;
         wt1 = m0 + 1 < nx ? a.wts[pair1] : 0.f;
         staged = pidx;
@@ -1156,12 +1179,12 @@ __global__ void __maxnreg__(120) moe_down_xs(const MoeArgs a, int stages, int pa
     const int pidx = static_cast<int>(i / tiles);
     if (pidx != staged) {
       named_bar_sync(1, kDnWarps * 32);
-      pr = moe_problem(a, probs, pidx);
+      pr = moe_problem<DIRECT>(a, probs, pidx);
       const int pieces = a.I / 8;
       for (int q = threadIdx.x; q < pr.nx * pieces; q += kDnWarps * 32) {
         const int m = q / pieces, pc = q - m * pieces;
         reinterpret_cast<uint4*>(xbuf + m * a.I * 2)[pc] =
-            __ldg(reinterpret_cast<const uint4*>(hbuf + static_cast<int64_t>(moe_pair(a, pairs, pr.first + m)) * a.I) + pc);
+            __ldg(reinterpret_cast<const uint4*>(hbuf + static_cast<int64_t>(moe_pair<DIRECT>(pairs, pr.first + m)) * a.I) + pc);
       }
       named_bar_sync(1, kDnWarps * 32);
 #pragma unroll
@@ -1205,34 +1228,42 @@ __global__ void __maxnreg__(120) moe_down_xs(const MoeArgs a, int stages, int pa
   }
 }
 
+// Whether the activation-stationary down kernel serves this layer.
+template <int FMT>
+bool moe_down_xs_ok(const MoeArgs& a) {
+  if (a.fmt != kQ4_0 && a.fmt != kQ8_0) return false;
+  if (a.I != kDnGroups * GemvFmt<FMT>::kGroupK || a.H % kDnItemRows != 0) return false;
+  if (reinterpret_cast<uintptr_t>(a.w_down) % 16 || a.rb_i % 16) return false;
+  const size_t fixed = kDnHeader + kDnRedBytes + size_t(8) * a.I * 2;
+  const size_t stage = size_t(kDnItemRows / 2) * (2 * static_cast<size_t>(a.rb_i) + 16);
+  return fixed + 3 * stage <= device_max_smem_optin();
+}
+
 template <int FMT>
 cudaError_t launch_moe_down_xs(const MoeArgs& a, cudaStream_t stream, bool* launched) {
   *launched = false;
-  if (a.fmt != kQ4_0 && a.fmt != kQ8_0) return cudaSuccess;
-  if (a.I != kDnGroups * GemvFmt<FMT>::kGroupK || a.H % kDnItemRows != 0) return cudaSuccess;
-  if (reinterpret_cast<uintptr_t>(a.w_down) % 16 || a.rb_i % 16) return cudaSuccess;
+  if (!moe_down_xs_ok<FMT>(a)) return cudaSuccess;
   const int pair_pitch = 2 * static_cast<int>(a.rb_i) + 16;
   const size_t fixed = kDnHeader + kDnRedBytes + size_t(8) * a.I * 2;
   const size_t avail = device_max_smem_optin();
   const size_t stage = size_t(kDnItemRows / 2) * pair_pitch;
-  if (fixed + 3 * stage > avail) return cudaSuccess;
   const int stages = static_cast<int>(std::min<size_t>(kDnMaxStages, (avail - fixed) / stage));
   const size_t smem = fixed + size_t(stages) * stage;
+  auto* kernel = a.direct ? moe_down_xs<FMT, true> : moe_down_xs<FMT, false>;
   int dev = 0;
   cudaGetDevice(&dev);
-  static std::atomic<bool> configured[64];
-  if (!configured[dev & 63].load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(moe_down_xs<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(avail));
+  static std::atomic<bool> configured[64][2];
+  if (!configured[dev & 63][a.direct ? 1 : 0].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(avail));
     if (e != cudaSuccess) return e;
-    configured[dev & 63].store(true, std::memory_order_release);
+    configured[dev & 63][a.direct ? 1 : 0].store(true, std::memory_order_release);
   }
   MoeArgs args = a;
   int st = stages, pp = pair_pitch;
   void* kargs[] = {&args, &st, &pp};
   *launched = true;
-  return launch_pdl(reinterpret_cast<const void*>(moe_down_xs<FMT>), dim3(device_sm_count()), dim3(kDnThreads), smem,
-                    stream, kargs);
+  return launch_pdl(reinterpret_cast<const void*>(kernel), dim3(device_sm_count()), dim3(kDnThreads), smem, stream,
+                    kargs);
 }
 
 template <int FMT>
@@ -1242,7 +1273,11 @@ cudaError_t moe_run(const MoeArgs& a0, cudaStream_t stream, const MoeEp* ep = nu
   // and a dependent step in front of the weight stream) is skipped; it
   // costs a second read of an expert's weights only when two of the pairs
   // pick the same expert.
-  args.direct = ep == nullptr && static_cast<int64_t>(a0.T) * a0.topk <= kMoeDirectPairs;
+  // Both expert kernels must be the activation-stationary ones (the grouped
+  // fallback reads the routed problem list).
+  if constexpr (FMT == kQ4_0 || FMT == kQ8_0)
+    args.direct = ep == nullptr && static_cast<int64_t>(a0.T) * a0.topk <= kMoeDirectPairs &&
+                  moe_gateup_xs_ok(a0) && moe_down_xs_ok<FMT>(a0);
   const MoeArgs& a = args;
   if (!a.direct) {
     void* kargs[] = {&args};
