@@ -20,8 +20,10 @@ bytes streamed per second (whole job, all ranks).
   order) and exits non-zero on a mismatch.
 * e2e: the same sweep through the public C-ABI with host buffers: every step
   copies that step's activations from pinned host memory and reads every
-  output back to pinned host memory inside the timed region.  Weights stay
-  resident (uploaded once, as at model load).
+  output back to pinned host memory inside the timed region, as a serving
+  loop does (double-buffered: the next step's upload and the previous step's
+  read-back run on two copy streams while this step's MUL_MATs run).
+  Weights stay resident (uploaded once, as at model load).
 * extras: every other BASELINE config with its own roofline object — the
   standalone dequant (configs 0/1, row-sharded at N > 1), the prefill GEMM
   (config 3, row-sharded plus an NCCL all-gather at N > 1), the MoE layer
@@ -415,21 +417,23 @@ class Timer:
     def __init__(self, dev, world, graph_steps, stream):
         self.dev, self.world, self.graph_steps, self.stream = dev, world, graph_steps, stream
 
-    def _capture(self, nsteps, body):
+    def _capture(self, nsteps, body, finish=None):
         import torch
 
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=self.stream):
             for j in range(nsteps):
                 body(j)
+            if finish is not None:
+                finish(nsteps)  # join side streams back into the capture stream
         return g
 
-    def prepare(self, nsteps, cache, body, gsteps):
+    def prepare(self, nsteps, cache, body, gsteps, finish=None):
         full, tail = divmod(nsteps, gsteps)
         if full and "main" not in cache:
-            cache["main"] = self._capture(gsteps, body)
+            cache["main"] = self._capture(gsteps, body, finish)
         if tail and ("tail", tail) not in cache:
-            cache[("tail", tail)] = self._capture(tail, body)
+            cache[("tail", tail)] = self._capture(tail, body, finish)
 
     def replay(self, nsteps, cache, gsteps):
         full, tail = divmod(nsteps, gsteps)
@@ -438,17 +442,18 @@ class Timer:
         if tail:
             cache[("tail", tail)].replay()
 
-    def timed(self, nsteps, warm, body, gsteps=None):
+    def timed(self, nsteps, warm, body, gsteps=None, finish=None):
         """Device ms of `nsteps` steps (max over ranks).  A graph holds
         `gsteps` steps (default: the headline's); make it a whole number of
-        the body's buffer-rotation cycles."""
+        the body's buffer-rotation cycles.  `finish(n)` runs at the end of
+        each capture (to join streams the body forked)."""
         import torch
         import torch.distributed as dist
 
         gsteps = gsteps or self.graph_steps
         cache = {}
-        self.prepare(warm, cache, body, gsteps)
-        self.prepare(nsteps, cache, body, gsteps)
+        self.prepare(warm, cache, body, gsteps, finish)
+        self.prepare(nsteps, cache, body, gsteps, finish)
         if self.world > 1:
             # fused exchanges wait on the device for at most 2 s: ranks start
             # the warm-up together
@@ -632,28 +637,55 @@ def run_spiral(args):
     # e2e through the public C-ABI with host buffers (pinned), copies in the
     # timed region every step: the step's activations (B = 1, 2, 4, 8 stacked
     # in one pinned buffer) go up in one copy, the four MUL_MATs write their
-    # outputs into one device buffer, which comes back in one copy
+    # outputs into one device buffer, which comes back in one copy.  Serving
+    # pipeline: device and host buffers alternate between steps, uploads run
+    # on one copy stream and read-backs on another, so step i + 1's upload and
+    # step i - 1's read-back overlap step i's MUL_MATs; event waits keep each
+    # buffer's upload, MUL_MATs and read-back in order.
     offs = np.cumsum([0] + list(BATCHES))
     rows = int(offs[-1])
     hx_all = torch.from_numpy(np.concatenate([F.gen_activations(B, K, seed=200 + B) for B in BATCHES]).view(np.int16))
     hx_all = hx_all.pin_memory()
-    hy_all = torch.empty((rows, N), dtype=torch.int16).pin_memory()
-    xd_all = torch.empty((rows, K), dtype=torch.bfloat16, device=dev)
-    yd_all = torch.empty((rows, N), dtype=torch.bfloat16, device=dev)
+    hy_all = [torch.empty((rows, N), dtype=torch.int16).pin_memory() for _ in range(2)]
+    xd_all = [torch.empty((rows, K), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    yd_all = [torch.empty((rows, N), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    s_up, s_down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
 
     def sweep_e2e(i):
-        xd_all.view(torch.int16).copy_(hx_all, non_blocking=True)
+        b = i % 2
+        cap = torch.cuda.current_stream()
+        # upload: buffer b is free once step i - 2's MUL_MATs are done
+        s_up.wait_stream(cap) if i < 2 else s_up.wait_event(ev_comp[b])
+        with torch.cuda.stream(s_up):
+            xd_all[b].view(torch.int16).copy_(hx_all, non_blocking=True)
+            ev_in[b].record(s_up)
+        cap.wait_event(ev_in[b])
+        if i >= 2:
+            cap.wait_event(ev_out[b])  # step i - 2's read-back of yd[b] is done
         for j, B in enumerate(BATCHES):
             w = weights[(i * len(BATCHES) + j) % copies]
-            xb, yb = xd_all[offs[j] : offs[j] + B], yd_all[offs[j] : offs[j] + B]
+            xb, yb = xd_all[b][offs[j] : offs[j] + B], yd_all[b][offs[j] : offs[j] + B]
             if world > 1:
                 sp.mul_mat_allgather(fid, w, xb, Nr, K, yb, n0, xc.peers, rank, world)
             else:
                 sp.mul_mat(fid, w, xb, Nr, K, yb, y_dtype=sp.BF16, static_weights=True)
-        hy_all.copy_(yd_all.view(torch.int16), non_blocking=True)
+        ev_comp[b].record(cap)
+        s_down.wait_event(ev_comp[b])
+        with torch.cuda.stream(s_down):
+            hy_all[b].copy_(yd_all[b].view(torch.int16), non_blocking=True)
+            ev_out[b].record(s_down)
+
+    def join_e2e(n):
+        cap = torch.cuda.current_stream()
+        for b in range(min(n, 2)):
+            cap.wait_event(ev_out[b])
+        cap.wait_stream(s_up)
 
     e2e_steps = max(graph_steps, args.steps // 4)
-    ms_e2e = timer.timed(e2e_steps, 3, sweep_e2e)
+    ms_e2e = timer.timed(e2e_steps, 3, sweep_e2e, finish=join_e2e)
     e2e_value = wbytes_step / (ms_e2e / e2e_steps * 1e-3) / 1e9
     h2d = sum(B * K * 2 for B in BATCHES)
     d2h = sum(B * N * 2 for B in BATCHES)
@@ -715,7 +747,9 @@ def run_spiral(args):
             "parity": parity,
             "roofline": head_roof,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "note": "public C-ABI; every step one pinned-host copy of the step's activations in and one of its outputs out; weights resident"},
+                    "note": "public C-ABI; every step one pinned-host copy of the step's activations in and one of its outputs out "
+                            "(double-buffered: uploads and read-backs on two copy streams overlap the neighbouring steps' "
+                            "MUL_MATs); weights resident"},
             "gpu_launches": args.steps * len(BATCHES),
             "clocks": clk.summary(),
         }
