@@ -107,3 +107,36 @@ def test_gemm_q6_k_tensor_core_path(cuda, M, N, K):
     assert ok, rel
     assert rel < 5e-5, rel  # fp32 accumulation over K up to 6144
     assert sp.device_status() == 0
+
+
+@pytest.mark.parametrize("fid", GEMM_FMTS, ids=lambda f: F.NAMES[f])
+def test_gemm_is_bitwise_repeatable(cuda, fid):
+    """Config 3's smallest shape (M = 512, N = 4096): repeated calls agree
+    bit for bit, eagerly and as several calls inside one CUDA graph, and a
+    sample of outputs is within the MUL_MAT tolerance."""
+    import torch
+
+    M, N, K = 512, 4096, 4096
+    raw = F.generate(fid, K, N, seed=9)
+    x = F.gen_activations(M, K, seed=10)
+    w, xd = dev_bytes(raw), dev_bf16(x)
+    first = sp.mul_mat(fid, w, xd, N, K, y_dtype=sp.F32).cpu().numpy()
+    for _ in range(3):
+        assert np.array_equal(sp.mul_mat(fid, w, xd, N, K, y_dtype=sp.F32).cpu().numpy(), first)
+    ys = [torch.empty((M, N), dtype=torch.float32, device="cuda") for _ in range(3)]
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for y in ys:
+            sp.mul_mat(fid, w, xd, N, K, y, y_dtype=sp.F32, stream=s)
+    g.replay()
+    torch.cuda.synchronize()
+    del g
+    for y in ys:
+        assert np.array_equal(y.cpu().numpy(), first)
+    rng = np.random.default_rng(1)
+    rows = np.sort(rng.choice(M, size=32, replace=False))
+    cols = np.sort(rng.choice(N, size=256, replace=False))
+    ok, rel = tolerance_ok(first[np.ix_(rows, cols)], _sampled_reference(fid, raw, x, K, N, rows, cols), bf16_out=False)
+    assert ok, rel
+    assert sp.device_status() == 0
