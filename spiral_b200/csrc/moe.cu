@@ -777,10 +777,13 @@ __global__ void __maxnreg__(96) moe_gateup_xs(const MoeArgs a, int stages, int p
     }
     abort_flag = 0;
     fence_mbar_init();
-    griddep_launch_dependents();
   }
   __syncthreads();
   griddep_wait();  // the route kernel wrote what follows
+  // The down kernel may start once every CTA is past this point: the problem
+  // list (or the ids) is then complete, so its producer can stream the down
+  // weights while this kernel still runs.
+  if (threadIdx.x == 0) griddep_launch_dependents();
 
   const int* hdr = reinterpret_cast<const int*>(a.ws + a.L.hdr);
   const int* pairs = reinterpret_cast<const int*>(a.ws + a.L.pairs);
@@ -1057,7 +1060,11 @@ __global__ void __maxnreg__(120) moe_down_xs(const MoeArgs a, int stages, int pa
     griddep_launch_dependents();
   }
   __syncthreads();
-  griddep_wait();  // the gate/up kernel wrote h
+  // The problem list and the weights are final when this kernel starts (the
+  // gate/up kernel releases it only after its own wait on the routing): the
+  // producer streams weights at once; the consumers and the reducer wait for
+  // the gate/up kernel to complete before reading h or writing outputs.
+  if (warp != kDnWarpProducer) griddep_wait();
 
   const int* hdr = reinterpret_cast<const int*>(a.ws + a.L.hdr);
   const int* pairs = reinterpret_cast<const int*>(a.ws + a.L.pairs);
