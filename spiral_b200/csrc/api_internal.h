@@ -78,6 +78,11 @@ __host__ __device__ constexpr int64_t gemv_xchg_slot_bytes(int64_t n_total) { re
 bool gemv_xs_ok(const MatArgs& a);
 cudaError_t gemv_xs(const MatArgs& a, const PeerOut* po, cudaStream_t stream);
 
+// gemv_xs6.cu — activation-stationary GEMV for Q6_K at K = 1536 with dense
+// 1260-byte rows and N a multiple of 32 (the Gemma output head shape).
+bool gemv_xs6_ok(const MatArgs& a);
+cudaError_t gemv_xs6(const MatArgs& a, cudaStream_t stream);
+
 // gemm.cu — tcgen05 dequant-GEMM for larger M.
 bool gemm_supported(const MatArgs& a);
 cudaError_t gemm(const MatArgs& a, cudaStream_t stream);

@@ -502,6 +502,9 @@ bool gemv_fast_ok(const MatArgs& a) {
 template <int FMT>
 static cudaError_t gemv_t(const MatArgs& a, cudaStream_t stream, const PeerOut* po = nullptr) {
   using F = GemvFmt<FMT>;
+  if constexpr (FMT == kQ6_K) {
+    if (po == nullptr && gemv_xs6_ok(a)) return gemv_xs6(a, stream);
+  }
   if (gemv_xs_ok(a)) return gemv_xs(a, po, stream);
   GemvPlan plan;
   if (!gemv_plan<FMT>(a, &plan) || (po != nullptr && plan.window)) {

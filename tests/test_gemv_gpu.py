@@ -271,17 +271,51 @@ def test_gathered_gemv_single_rank(cuda, fid):
     assert sp.device_status() == 0
 
 
-@pytest.mark.parametrize("M", [1, 8])
-def test_gemv_gemma_q6_k_output_head_shape(cuda, M):
+@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("N", [4096, 4100])
+def test_gemv_gemma_q6_k_output_head_shape(cuda, M, N):
     """The Gemma-style Q6_K output head (K = 1536: 1260-byte rows, not a
-    16-byte multiple) runs the pipelined GEMV with window copies."""
-    fid, K, N = F.Q6_K, 1536, 4096
+    16-byte multiple): N a multiple of 32 runs the six-super-block kernel
+    (four-row bulk copies), other N the pipelined GEMV with window copies."""
+    fid, K = F.Q6_K, 1536
     raw = F.generate(fid, K, N, seed=77)
     x = F.gen_activations(M, K, seed=78)
-    y = sp.mul_mat(fid, dev_bytes(raw), dev_bf16(x), N, K, y_dtype=sp.F32).cpu().numpy()
+    w, xd = dev_bytes(raw), dev_bf16(x)
+    y = sp.mul_mat(fid, w, xd, N, K, y_dtype=sp.F32).cpu().numpy()
     ok, rel = tolerance_ok(y, oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=False)
     assert ok, rel
     assert rel < 1e-5, rel
+    assert np.array_equal(sp.mul_mat(fid, w, xd, N, K, y_dtype=sp.F32).cpu().numpy(), y)
+    assert sp.device_status() == 0
+
+
+@pytest.mark.parametrize("ftz", [False, True])
+def test_gemv_gemma_head_strided_accumulate(cuda, ftz):
+    """Six-super-block kernel with activations at an odd row stride (scalar
+    fragment loads), an accumulating strided f32 output, subnormal scales
+    flushed or kept, and bf16 output."""
+    import torch
+
+    fid, K, N, M = F.Q6_K, 1536, 1024, 5
+    raw = F.generate(fid, K, N, seed=21)
+    blk = raw.reshape(-1, 210).copy()
+    blk[:6, 208:210] = np.array([0x0001, 0x8005, 0x03FF, 0x8000, 0x0000, 0x0200], dtype=np.uint16).view(np.uint8).reshape(-1, 2)
+    raw = blk.reshape(-1)
+    x = F.gen_activations(M, K, seed=22)
+    xbig = np.zeros((M, K + 3), dtype=np.uint16)
+    xbig[:, :K] = x
+    y = torch.full((M, N + 8), 0.5, dtype=torch.float32, device="cuda")
+    sp.mul_mat(fid, dev_bytes(raw), dev_bf16(xbig), N, K, y, y_dtype=sp.F32, x_row_stride=K + 3, y_row_stride=N + 8,
+               accumulate=True, ftz=ftz)
+    ref = oracle.mul_mat_f64(fid, raw, x, K, N, ftz=ftz)
+    got = y.cpu().numpy()
+    ok, rel = tolerance_ok(got[:, :N], ref + 0.5, bf16_out=False)
+    assert ok, rel
+    assert np.all(got[:, N:] == 0.5)
+    yb = host_bits(sp.mul_mat(fid, dev_bytes(raw), dev_bf16(x), N, K, y_dtype=sp.BF16, ftz=ftz))
+    ok, rel = tolerance_ok(F.bf16_bits_to_f32(yb), ref, bf16_out=True)
+    assert ok, rel
+    assert sp.device_status() == 0
 
 
 @pytest.mark.parametrize("fid", FMTS, ids=lambda f: F.NAMES[f])
