@@ -75,6 +75,7 @@ def parse_args(argv=None):
                          "(B from --batch), nothing else")
     ap.add_argument("--batch", type=int, default=1, help="activation vectors for --profile gemv / gemm, tokens for moe")
     ap.add_argument("--features", type=int, default=N_DIM, help="output features for --profile gemv / gemm")
+    ap.add_argument("--k", type=int, default=K_DIM, help="reduction dimension for --profile gemv / gemm / dequant")
     return ap.parse_args(argv)
 
 
@@ -489,7 +490,7 @@ def run_profile(args):
 
     torch.cuda.set_device(0)
     fid = F.BY_NAME[args.fmt]
-    K = K_DIM
+    K = args.k
     n = args.warmup + args.steps
     if args.profile == "moe":
         E, H, I, T = MOE_E, MOE_H, MOE_I, args.batch
