@@ -746,6 +746,13 @@ def run_spiral(args):
                             f"> 126 MB L2)",
                       "graphs": f"CUDA graphs of {graph_steps} steps, captured before the timed region"},
             "parity": parity,
+            "per_launch_us": {
+                "step": ms_per_step * 1e3 / len(BATCHES),
+                "kernel": launch_s * 1e6,
+                "gather": max(0.0, ms_per_step * 1e3 / len(BATCHES) - launch_s * 1e6) if world > 1 else 0.0,
+                "note": ("one MUL_MAT: the timed step per launch; at N > 1 the same sweep on the shard without the "
+                         "all-gather (kernel) and the difference (the fused gather's share)"),
+            },
             "roofline": head_roof,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "note": "public C-ABI; every step one pinned-host copy of the step's activations in and one of its outputs out "
