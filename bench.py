@@ -1016,9 +1016,33 @@ def bench_extras(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, tc_peak,
             alg = rbh * Nh + B * Kh * 2 + B * Nh * 2
             out["gemv"][f"q6_k_K{Kh}_N{Nh}_B{B}"] = {
                 "us": t * 1e6, "weight_GBps": rbh * Nh / t / 1e9,
-                "roofline": roofline("hbm", alg, t, hbm_peak, peak_kind, "gemv_kernel<q6_k> (window rows)",
+                "roofline": roofline("hbm", alg, t, hbm_peak, peak_kind, "gemv_xs6_kernel<q6_k> (six-super-block rows)",
                                      profile_traffic(f"gemv_q6_k_K{Kh}_N{Nh}_B{B}"))}
         del wh
+        # Gemma 4 E2B Q4_0 projections the reference lists for its first
+        # end-to-end target (K = 1536 / 2048; N = 256 .. 12288): small
+        # matrices, so a launch's fixed cost weighs in
+        fid = F.Q4_0
+        for Ke, Ne in ((1536, 256), (1536, 2048), (1536, 6144), (1536, 12288), (2048, 1536)):
+            rbe = F.row_bytes(fid, Ke)
+            raw = F.generate(fid, Ke, Ne, seed=0)
+            copies = min(2048, max(8, math.ceil(2 * L2_BYTES / (rbe * Ne))))  # > 2x L2 in all
+            w0 = torch.from_numpy(raw).to(dev)
+            ws = [w0] + [w0.clone() for _ in range(copies - 1)]
+            for B in (1, 8):
+                x = torch.from_numpy(F.gen_activations(B, Ke, seed=B).view(np.int16)).to(dev).view(torch.bfloat16)
+                y = torch.empty((B, Ne), dtype=torch.bfloat16, device=dev)
+
+                def body_e(i, ws=ws, x=x, y=y, Ke=Ke, Ne=Ne, copies=copies):
+                    sp.mul_mat(fid, ws[i % copies], x, Ne, Ke, y, y_dtype=sp.BF16, static_weights=True)
+
+                t = timer.timed(copies, 3, body_e, gsteps=copies) / copies * 1e-3
+                alg = rbe * Ne + B * Ke * 2 + B * Ne * 2
+                out["gemv"][f"q4_0_K{Ke}_N{Ne}_B{B}"] = {
+                    "us": t * 1e6, "weight_GBps": rbe * Ne / t / 1e9,
+                    "roofline": roofline("hbm", alg, t, hbm_peak, peak_kind, "gemv<q4_0> (Gemma 4 E2B shape)",
+                                         profile_traffic(f"gemv_q4_0_K{Ke}_N{Ne}_B{B}"))}
+            del ws, w0
     out["dequant"] = bench_dequant(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_kind)
     out["gemm"] = bench_gemm(sp, F, dev, rank, world, timer, hbm_peak, tc_peak, peak_kind)
     out["moe"] = bench_moe(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_kind)
