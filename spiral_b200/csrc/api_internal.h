@@ -71,8 +71,9 @@ cudaError_t gemv_allgather(const MatArgs& a, const PeerOut& po, cudaStream_t str
 constexpr int64_t kGemvXchgCtrlBytes = 256;
 __host__ __device__ constexpr int64_t gemv_xchg_slot_bytes(int64_t n_total) { return 8 * n_total * 4; }
 
-// gemv_xs.cu — activation-stationary GEMV for Q4_0 / Q8_0 at K in {1024,
-// 2048, 4096}; gemv() and gemv_allgather() use it whenever it applies.
+// gemv_xs.cu — activation-stationary GEMV for Q4_0 / Q8_0 at K in {1536,
+// 2048, 3072, 4096} and Q6_K at K = 4096; gemv() and gemv_allgather() use it
+// whenever it applies.
 // po == nullptr: plain MUL_MAT; else the row-sharded call with the
 // all-gather fused in (same exchange protocol as above).
 bool gemv_xs_ok(const MatArgs& a);

@@ -1,13 +1,13 @@
 // gemv_xs.cu — activation-stationary dequant-GEMV (decode, M <= 8) on
 // sm_100a: the fast path of the quantized MUL_MAT (reference unpack_mmul,
 // src/quants/q4_0/mmul.aie.h:16-90, q8_0/mmul.aie.h:16-117,
-// q6_k/mmul.aie.h:18-84) for Q4_0 / Q8_0 at K in {2048, 4096} and Q6_K at
-// K = 4096:
+// q6_k/mmul.aie.h:18-84) for Q4_0 / Q8_0 at K in {1536, 2048, 3072, 4096}
+// and Q6_K at K = 4096 (K = NW warps x GPW decode groups, NW = 16 or 12):
 //
 //   y[m][n] = sum_k bf16(W[n][k]) * x[m][k]      (fp32 accumulate)
 //
-// Structure (one persistent CTA per SM: 16 consumer warps and a producer
-// warp):
+// Structure (one persistent CTA per SM: NW consumer warps, a producer and a
+// reducer warp):
 //  * A tile is 16 output features; tiles are dealt to CTAs round-robin.
 //    The producer warp streams the weights: 8 of its lanes each issue one
 //    1-D bulk copy of a pair of consecutive rows (rows are contiguous in the
@@ -17,13 +17,13 @@
 //    issued them held every reduction back by microseconds).  Pairs sit at a pitch
 //    of 2 rows + 16 bytes, and MMA row g (g + 8) is weight row 2g (2g + 1),
 //    so the 8 rows a fragment load touches lie in different banks.
-//  * Warp w owns the fixed K slice [w*K/16, (w+1)*K/16) of every tile.  Its
+//  * Warp w owns the fixed K slice [w*K/NW, (w+1)*K/NW) of every tile.  Its
 //    activation fragments (the B operands of all its mma.sync.m16n8k16 steps)
 //    are loaded once, at kernel start, straight from global x into registers
 //    (bf16, the exact inputs: nothing is converted).  Per tile the warp
 //    decodes its slice with the exact decoders of gemv_decode.cuh (A
 //    fragments hold bf16_rne(d * q), bit for bit the standalone dequant) and
-//    the 16 warps' partial 16x8 tiles are summed in warp order by a reducer
+//    the NW warps' partial 16x8 tiles are summed in warp order by a reducer
 //    warp of its own through a double-buffered shared array, handed over with
 //    mbarriers, so decoding warps never wait for a reduction (reductions done
 //    by rotating sets of the decoding warps cost about 0.3 us per tile: the
@@ -40,13 +40,21 @@
 namespace spiral {
 namespace {
 
-constexpr int kXsWarps = 16;  // consumer warps: warp w owns K slice w
-constexpr int kXsWarpProducer = kXsWarps, kXsWarpReducer = kXsWarps + 1;
-constexpr int kXsThreads = (kXsWarps + 2) * 32;  // + the producer and the reducer warp
+// NW consumer warps (16, or 12 for K of 12 decode groups: 1536 / 3072): warp
+// w owns K slice w; then the producer and the reducer warp.
+template <int NW>
+struct XsWarps {
+  static constexpr int kProducer = NW, kReducer = NW + 1;
+  static constexpr int kThreads = (NW + 2) * 32;
+  static constexpr int kRedBytes = 2 * NW * 32 * 16;
+  // 18 warps spread 5 + 5 + 4 + 4 over the sub-partitions: 96 registers per
+  // thread is the most that launches; 14 warps (4 + 4 + 3 + 3) allow 128
+  static constexpr int kMaxRegs = NW > 14 ? 96 : 128;
+};
 constexpr int kXsRows = 16;  // tile height (MMA M)
 constexpr int kXsMaxStages = 8;
 constexpr int kXsHeader = 2048;  // barriers and abort word; gathered-tile staging at 1024
-constexpr int kXsRedBytes = 2 * kXsWarps * 32 * 16;
+constexpr int kXsRedBytes = 2 * 16 * 32 * 16;  // the largest (NW = 16)
 constexpr int kXsBarConsumers = 1;  // named barrier of the consumer warps
 
 struct XsParams {
@@ -89,11 +97,10 @@ __device__ __forceinline__ bool xs_wait(uint64_t* bar, uint32_t parity, int& abo
 // Weight row of MMA row R of a tile.
 __device__ __forceinline__ int xs_weight_row(int R) { return R < 8 ? 2 * R : 2 * (R - 8) + 1; }
 
-template <int FMT, int GPW, bool GATHER, bool FTZ>
-// 18 warps are spread 5 + 5 + 4 + 4 over the sub-partitions, each with a
-// quarter of the register file: 96 registers per thread is the most that
-// launches.
-__global__ void __maxnreg__(96) gemv_xs_kernel(const XsParams p) {
+template <int FMT, int GPW, bool GATHER, bool FTZ, int NW>
+__global__ void __maxnreg__(XsWarps<NW>::kMaxRegs) gemv_xs_kernel(const XsParams p) {
+  constexpr int kXsWarps = NW;
+  constexpr int kXsWarpProducer = XsWarps<NW>::kProducer, kXsWarpReducer = XsWarps<NW>::kReducer;
   using F = GemvFmt<FMT>;
   constexpr int kSteps = F::kSteps;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -383,25 +390,33 @@ __global__ void __maxnreg__(96) gemv_xs_kernel(const XsParams p) {
   }
 }
 
-// Groups per warp (K = 16 warps x GPW groups); 0 = not served here.
-int xs_gpw(const MatArgs& a) {
-  if (a.fmt == kQ6_K) return a.K == 4096 ? 1 : 0;
-  if (a.fmt == kQ4_0 || a.fmt == kQ8_0) {
-    if (a.K == 2048) return 1;
-    if (a.K == 4096) return 2;
+// Consumer warps and groups per warp (K = NW warps x GPW groups of kGroupK);
+// false = not served here.
+bool xs_shape(const MatArgs& a, int* nw, int* gpw) {
+  const int gk = a.fmt == kQ6_K ? 256 : 128;
+  if (a.fmt != kQ4_0 && a.fmt != kQ8_0 && a.fmt != kQ6_K) return false;
+  if (a.K % gk != 0) return false;
+  const int64_t groups = a.K / gk;
+  const int max_gpw = a.fmt == kQ6_K ? 1 : 2;
+  for (int w : {16, 12}) {
+    if (groups % w == 0 && groups / w <= max_gpw) {
+      *nw = w;
+      *gpw = static_cast<int>(groups / w);
+      return true;
+    }
   }
-  return 0;
+  return false;
 }
 
 struct XsPlan {
-  int gpw = 0, row_bytes = 0, pair_pitch = 0, stages = 0;
+  int nw = 0, gpw = 0, row_bytes = 0, pair_pitch = 0, stages = 0;
   size_t smem = 0;
 };
 
 bool xs_plan(const MatArgs& a, XsPlan* out) {
   if (a.M < 1 || a.M > 8) return false;
-  const int gpw = xs_gpw(a);
-  if (gpw == 0) return false;
+  int nw = 0, gpw = 0;
+  if (!xs_shape(a, &nw, &gpw)) return false;
   if (reinterpret_cast<uintptr_t>(a.w) % 16 != 0 || a.w_stride % 16 != 0) return false;
   const int bk = a.fmt == kQ6_K ? 256 : 32, bb = a.fmt == kQ4_0 ? 18 : (a.fmt == kQ8_0 ? 34 : 210);
   const int row_bytes = static_cast<int>(a.K / bk) * bb;  // a multiple of 16 for the K served
@@ -410,6 +425,7 @@ bool xs_plan(const MatArgs& a, XsPlan* out) {
   const size_t avail = device_max_smem_optin();
   const size_t stage = size_t(8) * pair_pitch;
   if (fixed + 2 * stage > avail) return false;
+  out->nw = nw;
   out->gpw = gpw;
   out->row_bytes = row_bytes;
   out->pair_pitch = pair_pitch;
@@ -418,15 +434,15 @@ bool xs_plan(const MatArgs& a, XsPlan* out) {
   return true;
 }
 
-template <int FMT, int GPW>
+template <int FMT, int GPW, int NW>
 cudaError_t xs_launch_t(const XsParams& p, bool gather, bool ftz, size_t smem, cudaStream_t stream) {
-  auto* kernel = gather ? (ftz ? gemv_xs_kernel<FMT, GPW, true, true> : gemv_xs_kernel<FMT, GPW, true, false>)
-                        : (ftz ? gemv_xs_kernel<FMT, GPW, false, true> : gemv_xs_kernel<FMT, GPW, false, false>);
+  auto* kernel = gather ? (ftz ? gemv_xs_kernel<FMT, GPW, true, true, NW> : gemv_xs_kernel<FMT, GPW, true, false, NW>)
+                        : (ftz ? gemv_xs_kernel<FMT, GPW, false, true, NW> : gemv_xs_kernel<FMT, GPW, false, false, NW>);
   int dev = 0;
   cudaGetDevice(&dev);
   const int fslot = FMT == kQ4_0 ? 0 : (FMT == kQ8_0 ? 1 : 2);
-  const int slot = ((fslot * 2 + (GPW - 1)) * 2 + gather) * 2 + ftz;
-  static std::atomic<bool> configured[64][24];
+  const int slot = (((fslot * 2 + (GPW - 1)) * 2 + gather) * 2 + ftz) * 2 + (NW == 16 ? 0 : 1);
+  static std::atomic<bool> configured[64][48];
   if (!configured[dev & 63][slot].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(device_max_smem_optin()));
@@ -436,7 +452,7 @@ cudaError_t xs_launch_t(const XsParams& p, bool gather, bool ftz, size_t smem, c
   const int64_t tiles = (p.N + kXsRows - 1) / kXsRows;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(tiles, int64_t(device_sm_count()))));
-  cfg.blockDim = dim3(kXsThreads);
+  cfg.blockDim = dim3(XsWarps<NW>::kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -484,15 +500,23 @@ cudaError_t gemv_xs(const MatArgs& a, const PeerOut* po, cudaStream_t stream) {
     p.world = po->world;
   }
   const bool gather = po != nullptr;
+  const bool w16 = plan.nw == 16;
   switch (a.fmt) {
     case kQ4_0:
-      return plan.gpw == 1 ? xs_launch_t<kQ4_0, 1>(p, gather, a.ftz, plan.smem, stream)
-                           : xs_launch_t<kQ4_0, 2>(p, gather, a.ftz, plan.smem, stream);
+      if (plan.gpw == 1)
+        return w16 ? xs_launch_t<kQ4_0, 1, 16>(p, gather, a.ftz, plan.smem, stream)
+                   : xs_launch_t<kQ4_0, 1, 12>(p, gather, a.ftz, plan.smem, stream);
+      return w16 ? xs_launch_t<kQ4_0, 2, 16>(p, gather, a.ftz, plan.smem, stream)
+                 : xs_launch_t<kQ4_0, 2, 12>(p, gather, a.ftz, plan.smem, stream);
     case kQ8_0:
-      return plan.gpw == 1 ? xs_launch_t<kQ8_0, 1>(p, gather, a.ftz, plan.smem, stream)
-                           : xs_launch_t<kQ8_0, 2>(p, gather, a.ftz, plan.smem, stream);
+      if (plan.gpw == 1)
+        return w16 ? xs_launch_t<kQ8_0, 1, 16>(p, gather, a.ftz, plan.smem, stream)
+                   : xs_launch_t<kQ8_0, 1, 12>(p, gather, a.ftz, plan.smem, stream);
+      return w16 ? xs_launch_t<kQ8_0, 2, 16>(p, gather, a.ftz, plan.smem, stream)
+                 : xs_launch_t<kQ8_0, 2, 12>(p, gather, a.ftz, plan.smem, stream);
     case kQ6_K:
-      return xs_launch_t<kQ6_K, 1>(p, gather, a.ftz, plan.smem, stream);
+      return w16 ? xs_launch_t<kQ6_K, 1, 16>(p, gather, a.ftz, plan.smem, stream)
+                 : xs_launch_t<kQ6_K, 1, 12>(p, gather, a.ftz, plan.smem, stream);
   }
   return cudaErrorNotSupported;
 }

@@ -333,3 +333,32 @@ def test_gemv_rows_off_16_byte_alignment(cuda, fid):
     y = sp.mul_mat(fid, w, dev_bf16(x), N, K, y_dtype=sp.F32, w_row_stride=stride).cpu().numpy()
     ok, rel = tolerance_ok(y, oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=False)
     assert ok, rel
+
+
+@pytest.mark.parametrize("fid", [F.Q4_0, F.Q8_0], ids=lambda f: F.NAMES[f])
+@pytest.mark.parametrize("K", [1536, 3072])
+def test_gemv_twelve_warp_shapes(cuda, fid, K):
+    """K of 12 decode groups (1536 / 3072: the Gemma 4 E2B hidden size and
+    twice it) run the activation-stationary GEMV with 12 decoding warps:
+    within the MUL_MAT tolerance for several batch sizes and a ragged last
+    tile, repeatable, and the gathered call (world = 1) equal to the plain
+    call bit for bit."""
+    import torch
+
+    N = 1000
+    raw = F.generate(fid, K, N, seed=K + 3)
+    w = dev_bytes(raw)
+    for M in (1, 5, 8):
+        x = F.gen_activations(M, K, seed=M + K)
+        xd = dev_bf16(x)
+        y = sp.mul_mat(fid, w, xd, N, K, y_dtype=sp.F32).cpu().numpy()
+        ok, rel = tolerance_ok(y, oracle.mul_mat_f64(fid, raw, x, K, N), bf16_out=False)
+        assert ok, (M, rel)
+        assert np.array_equal(sp.mul_mat(fid, w, xd, N, K, y_dtype=sp.F32).cpu().numpy(), y)
+        yb = sp.mul_mat(fid, w, xd, N, K, y_dtype=sp.BF16)
+        yg = torch.zeros((M, N), dtype=torch.bfloat16, device="cuda")
+        xchg = torch.zeros(sp.allgather_exchange_bytes(N), dtype=torch.uint8, device="cuda")
+        peers = torch.tensor([xchg.data_ptr()], dtype=torch.int64, device="cuda")
+        sp.mul_mat_allgather(fid, w, xd, N, K, yg, 0, peers, 0, 1)
+        assert torch.equal(yg.view(torch.int16), yb.view(torch.int16))
+    assert sp.device_status() == 0
