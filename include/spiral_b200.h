@@ -247,8 +247,16 @@ SPIRAL_API int spiral_mul_mat(int fmt, const void* w, int64_t w_row_stride_bytes
  * the others' bounded waits (2 s) give up with bit 8 of spiral_device_status;
  * the ranks' call counts then disagree, so later calls skip their waits
  * until the status is read, and the exchanges must be zeroed again on every
- * rank before further use. */
+ * rank before further use (spiral_allgather_exchange_reset).  The gathered
+ * columns of every call since the timeout are invalid; each rank's own
+ * columns are complete. */
 SPIRAL_API int64_t spiral_allgather_exchange_bytes(int64_t N_total);
+/* Zero this rank's exchange buffer on the stream, as before the first call:
+ * the recovery after a peer timeout.  Peers read and write this buffer, so
+ * every rank first finishes its calls on the exchange (stream synchronize,
+ * then a host barrier), resets its own exchange, and the ranks meet at a
+ * host barrier again before the next gathered call. */
+SPIRAL_API int spiral_allgather_exchange_reset(void* exchange, int64_t N_total, void* stream);
 SPIRAL_API int spiral_mul_mat_allgather(int fmt, const void* w_shard, int64_t w_row_stride_bytes,
                                         const void* x, int64_t x_row_stride_elems,
                                         void* y, int64_t y_row_stride_elems, int64_t n_offset,
@@ -335,6 +343,10 @@ SPIRAL_API int spiral_moe_ffn(int fmt, const void* w_gate, const void* w_up, con
 /* Bytes of one rank's exchange buffer for spiral_moe_ffn_ep (0 if invalid:
  * non-positive dims).  Sized for up to max_tokens tokens per call. */
 SPIRAL_API int64_t spiral_moe_ep_exchange_bytes(int64_t hidden, int64_t max_tokens);
+/* Zero this rank's spiral_moe_ffn_ep exchange buffer on the stream, as
+ * before the first call: the recovery after a peer timeout, with the same
+ * barriers around it as spiral_allgather_exchange_reset. */
+SPIRAL_API int spiral_moe_ep_exchange_reset(void* exchange, int64_t hidden, int64_t max_tokens, void* stream);
 
 /* Expert-parallel MoE FFN layer, one process per GPU (BASELINE config 4 at
  * 2..8 GPUs; the reference has no MoE and no multi-device path, its

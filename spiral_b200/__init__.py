@@ -51,12 +51,14 @@ _SIGNATURES = {
     "spiral_ggml_mul_mat": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _u32, _vp], _i32),
     "spiral_quants_unpack_mmul_all": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _u32, _vp], _i32),
     "spiral_allgather_exchange_bytes": ([_i64], _i64),
+    "spiral_allgather_exchange_reset": ([_vp, _i64, _vp], _i32),
     "spiral_mul_mat_allgather": ([_i32, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i32,
                                   _i32, _u32, _vp], _i32),
     "spiral_moe_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64], _i64),
     "spiral_moe_ffn": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i32,
                         _i64, _vp, _i64, _u32, _vp], _i32),
     "spiral_moe_ep_exchange_bytes": ([_i64, _i64], _i64),
+    "spiral_moe_ep_exchange_reset": ([_vp, _i64, _i64, _vp], _i32),
     "spiral_moe_ffn_ep": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp,
                            _i32, _i64, _vp, _i32, _i32, _vp, _i64, _u32, _vp], _i32),
     "spiral_moe_ffn_noalloc": ([_i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp,
@@ -246,6 +248,13 @@ def allgather_exchange_bytes(n_total: int) -> int:
     return int(lib().spiral_allgather_exchange_bytes(n_total))
 
 
+def allgather_exchange_reset(exchange, n_total: int, *, stream=None) -> None:
+    """Zero this rank's exchange buffer (a device tensor) on the stream:
+    the recovery after a gathered wait timed out.  Every rank resets its own,
+    then the ranks meet at a barrier before the next gathered call."""
+    _check(lib().spiral_allgather_exchange_reset(_ptr(exchange), n_total, _stream(stream)))
+
+
 def mul_mat_allgather(fmt, w_shard, x, N_shard: int, K: int, y, n_offset: int, exchange_peers_dev, rank: int,
                       world: int, *, w_row_stride: int | None = None, ftz: bool = False, static_weights: bool = True,
                       stream=None):
@@ -299,6 +308,12 @@ def moe_ffn(fmt, w_gate, w_up, w_down, x, expert_ids, expert_weights, *, hidden:
 
 def moe_ep_exchange_bytes(hidden: int, max_tokens: int) -> int:
     return int(lib().spiral_moe_ep_exchange_bytes(hidden, max_tokens))
+
+
+def moe_ep_exchange_reset(exchange, hidden: int, max_tokens: int, *, stream=None) -> None:
+    """Zero this rank's moe_ffn_ep exchange buffer on the stream (the
+    recovery after a timed-out wait; every rank resets, then a barrier)."""
+    _check(lib().spiral_moe_ep_exchange_reset(_ptr(exchange), hidden, max_tokens, _stream(stream)))
 
 
 def moe_ffn_ep(fmt, w_gate, w_up, w_down, x, expert_ids, expert_weights, *, hidden: int, inter: int,

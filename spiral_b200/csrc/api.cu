@@ -326,6 +326,16 @@ int64_t spiral_allgather_exchange_bytes(int64_t N_total) {
   return gemv_xchg_bytes(N_total);
 }
 
+int spiral_allgather_exchange_reset(void* exchange, int64_t N_total, void* stream) {
+  g_last_error[0] = 0;
+  const int64_t bytes = spiral_allgather_exchange_bytes(N_total);
+  if (bytes == 0) return fail(SPIRAL_ERR_INVALID_SHAPE, "N_total=%lld: not a positive multiple of 8", (long long)N_total);
+  if (!exchange) return fail(SPIRAL_ERR_NULL_POINTER, "null exchange");
+  const cudaError_t e = cudaMemsetAsync(exchange, 0, static_cast<size_t>(bytes), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(SPIRAL_ERR_CUDA, "exchange reset: %s", cudaGetErrorString(e));
+  return SPIRAL_OK;
+}
+
 int spiral_mul_mat_allgather(int fmt, const void* w_shard, int64_t w_row_stride_bytes, const void* x,
                              int64_t x_row_stride_elems, void* y, int64_t y_row_stride_elems, int64_t n_offset,
                              int64_t M, int64_t N_shard, int64_t N_total, int64_t K, void* const* exchange_peers,
@@ -423,6 +433,17 @@ int spiral_moe_ffn(int fmt, const void* w_gate, const void* w_up, const void* w_
 int64_t spiral_moe_ep_exchange_bytes(int64_t hidden, int64_t max_tokens) {
   if (hidden <= 0 || max_tokens <= 0 || max_tokens > (int64_t(1) << 24) || hidden > (int64_t(1) << 20)) return 0;
   return moe_ep_xchg_bytes(hidden, max_tokens);
+}
+
+int spiral_moe_ep_exchange_reset(void* exchange, int64_t hidden, int64_t max_tokens, void* stream) {
+  g_last_error[0] = 0;
+  const int64_t bytes = spiral_moe_ep_exchange_bytes(hidden, max_tokens);
+  if (bytes == 0)
+    return fail(SPIRAL_ERR_INVALID_SHAPE, "hidden=%lld max_tokens=%lld", (long long)hidden, (long long)max_tokens);
+  if (!exchange) return fail(SPIRAL_ERR_NULL_POINTER, "null exchange");
+  const cudaError_t e = cudaMemsetAsync(exchange, 0, static_cast<size_t>(bytes), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(SPIRAL_ERR_CUDA, "exchange reset: %s", cudaGetErrorString(e));
+  return SPIRAL_OK;
 }
 
 int spiral_moe_ffn_ep(int fmt, const void* w_gate, const void* w_up, const void* w_down, int64_t n_experts_local,

@@ -122,12 +122,24 @@ class AllGatherExchange:
         if nbytes <= 0:
             raise ValueError("n_total must be a positive multiple of 8")
         self.n_total = n_total
+        self._group = group
         self._buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
         self._buf.zero_()
         self._hdl = symm_mem.rendezvous(self._buf, group=group if group is not None else dist.group.WORLD)
         self.peers = torch.tensor(list(self._hdl.buffer_ptrs), dtype=torch.int64, device=device)
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
+
+    def reset(self) -> None:
+        """Collective: zero every rank's exchange again, as after a gathered
+        wait timed out (device status bit 8); calls after it start afresh."""
+        from . import allgather_exchange_reset
+
+        torch.cuda.synchronize(self._buf.device)  # no call of any rank still in flight
+        dist.barrier(group=self._group)
+        allgather_exchange_reset(self._buf, self.n_total)
+        torch.cuda.synchronize(self._buf.device)
+        dist.barrier(group=self._group)
 
 
 class MoeExchange:
@@ -146,9 +158,21 @@ class MoeExchange:
         if nbytes <= 0:
             raise ValueError("hidden and max_tokens must be positive")
         self.hidden, self.max_tokens = hidden, max_tokens
+        self._group = group
         self._buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
         self._buf.zero_()
         self._hdl = symm_mem.rendezvous(self._buf, group=group if group is not None else dist.group.WORLD)
         self.peers = torch.tensor(list(self._hdl.buffer_ptrs), dtype=torch.int64, device=device)
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
+
+    def reset(self) -> None:
+        """Collective: zero every rank's exchange again, as after a timed-out
+        wait (device status bit 8)."""
+        from . import moe_ep_exchange_reset
+
+        torch.cuda.synchronize(self._buf.device)  # no call of any rank still in flight
+        dist.barrier(group=self._group)
+        moe_ep_exchange_reset(self._buf, self.hidden, self.max_tokens)
+        torch.cuda.synchronize(self._buf.device)
+        dist.barrier(group=self._group)

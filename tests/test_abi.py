@@ -195,6 +195,9 @@ def test_mul_mat_allgather_validation_codes():
     assert call(off=7164, N=7172) == -4  # 8-column granularity
     assert call(ys=14340) == -4
     assert call(y=264) == -4
+    # the recovery reset checks its arguments before touching the device
+    assert L.spiral_allgather_exchange_reset(256, 14332, 0) == -2
+    assert L.spiral_allgather_exchange_reset(0, 14336, 0) == -3
 
 
 def test_repack_rejects_misaligned_input_with_zero():
@@ -230,6 +233,8 @@ def test_moe_ep_validates_its_arguments():
     assert call(T=5) == -5  # more tokens than the exchange holds
     assert call(H=2048, world=3) == -2  # hidden not a multiple of world
     assert sp.moe_ep_exchange_bytes(0, 4) == 0 and sp.moe_ep_exchange_bytes(H, 4) > 0
+    assert L.spiral_moe_ep_exchange_reset(p, 0, 4, 0) == -2
+    assert L.spiral_moe_ep_exchange_reset(0, H, 4, 0) == -3
 
 
 def test_ggml_supports_mul_mat_follows_ggml_rules():

@@ -4,12 +4,14 @@ rank is a process with its own GPU running libspiral_b200.
 * dense row-sharded MUL_MAT (BASELINE config 2 dims, 14336 x 4096 Q4_0):
   NCCL all-gather, and the all-gather fused into the GEMV (flagged NVLink
   units): equal bit for bit to spiral_mul_mat on the whole weight, on every
-  rank, for B = 1, 2, 5, 8 and several calls through one exchange; checked
-  against the float64 oracle once;
+  rank, for B = 1, 2, 5, 8 and several calls through one exchange, before
+  and after the exchange's recovery reset; checked against the float64
+  oracle once;
 * expert-parallel MoE layer (BASELINE config 4 dims: 128 Q4_0 experts,
   hidden 2048, inter 768, top-8, T = 1 and 64) through spiral_moe_ffn_ep
   (combine fused over NVLink): identical on every rank and within the MoE
-  tolerance of the float64 oracle of the whole layer;
+  tolerance of the float64 oracle of the whole layer, the last call after
+  the exchange's recovery reset;
 The fused exchanges wait on the device for at most 2 s, so the ranks enter
 each one together (a barrier after every host-side oracle check).
 * the Python NCCL all-to-all dispatch/combine (spiral_b200.dist) at toy dims.
@@ -102,6 +104,9 @@ def _worker(rank, world, port, q):
                 # the ranks enter every exchange together: its device waits
                 # give up after 2 s, and the oracle above takes longer
                 dist.barrier()
+                # the recovery reset (collective): the calls after it start
+                # from a zeroed exchange and must still match bit for bit
+                xc.reset()
         res["fused_mismatch"] = mism
         torch.cuda.synchronize()
         dist.barrier()
@@ -116,7 +121,9 @@ def _worker(rank, world, port, q):
         wu_l = torch.from_numpy(np.concatenate([F.generate(fid, H, I, seed=12000 + e) for e in range(e0, e1)])).to(dev)
         wd_l = torch.from_numpy(np.concatenate([F.generate(fid, I, H, seed=13000 + e) for e in range(e0, e1)])).to(dev)
         mx = MoeExchange(H, 64, dev)
-        for T in (1, 64, 1):
+        for i, T in enumerate((1, 64, 1)):
+            if i == 2:
+                mx.reset()  # the last call starts from a zeroed exchange
             xm = F.gen_activations(T, H, seed=500 + T)
             ids, wts = F.gen_routing(T, E, topk, seed=600 + T)
             xmd = torch.from_numpy(xm.view(np.int16)).to(dev).view(torch.bfloat16).view(T, H)

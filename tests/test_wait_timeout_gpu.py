@@ -7,7 +7,8 @@ limit, for the other ranks' pieces of its output.  Here rank 0 of a world of
 (SPIRAL_ERR_TIMEOUT from spiral_device_status) and end the kernel, leaving
 the context usable.  The rank's own columns are still complete and correct,
 and a call made while the error bit is set skips its wait instead of waiting
-out the limit again.  Nothing faults or hangs: the wait is the kernel's own
+out the limit again; spiral_allgather_exchange_reset zeroes the exchange
+for the recovery.  Nothing faults or hangs: the wait is the kernel's own
 bounded poll of a flag that nothing sets.
 """
 
@@ -71,6 +72,11 @@ def test_gathered_wait_gives_up_and_reports_timeout(cuda):
     got = y[:, :N_shard].float().cpu().numpy()
     ok, rel = tolerance_ok(got, ref, bf16_out=True)
     assert ok, rel
+    # recovery: the exchange (call count, flags, pieces) is zeroed again
+    assert bool(own.any())
+    sp.allgather_exchange_reset(own, N_total)
+    torch.cuda.synchronize()
+    assert not bool(own.any())
     # the context is still usable: an ordinary MUL_MAT right after
     y2 = sp.mul_mat(fid, w_shard, xd, N_shard, K, y_dtype=sp.F32).cpu().numpy()
     ok, rel = tolerance_ok(y2, ref, bf16_out=False)
