@@ -512,6 +512,31 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
   }
 }
 
+// Sum over token t's slots j whose expert is local, in slot order, of
+// part[t*topk + j][n] (0 + the first such value, then the next, ...).  A
+// chunk of 8 slots issues all its id and partial loads before the adds, so a
+// thread waits about two memory latencies per chunk instead of two per slot.
+__device__ __forceinline__ float moe_local_slot_sum(const MoeArgs& a, const float* part, int64_t t, int64_t n) {
+  const int* ids = a.ids + t * a.topk;
+  const float* pt = part + t * a.topk * static_cast<int64_t>(a.H) + n;
+  float sum = 0.f;
+  for (int j0 = 0; j0 < a.topk; j0 += 8) {
+    float v[8];
+    bool use[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u;
+      const int ex = j < a.topk ? ids[j] - a.e0 : -1;
+      use[u] = ex >= 0 && ex < a.E_local;
+      v[u] = use[u] ? pt[static_cast<int64_t>(j) * a.H] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (use[u]) sum += v[u];
+  }
+  return sum;
+}
+
 // y[t][n] = sum over local slots j (in order) of part[t*topk + j][n].
 __global__ void moe_combine(const MoeArgs a) {
   griddep_launch_dependents();
@@ -521,12 +546,7 @@ __global__ void moe_combine(const MoeArgs a) {
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int t = static_cast<int>(e / a.H), n = static_cast<int>(e % a.H);
-    float sum = 0.f;
-    for (int j = 0; j < a.topk; ++j) {
-      const int pair = t * a.topk + j;
-      const int ex = a.ids[pair] - a.e0;
-      if (ex >= 0 && ex < a.E_local) sum += part[static_cast<int64_t>(pair) * a.H + n];
-    }
+    const float sum = moe_local_slot_sum(a, part, t, n);
     const int64_t off = static_cast<int64_t>(t) * a.y_stride + n;
     if (a.y_bf16) {
       static_cast<uint16_t*>(a.y)[off] = static_cast<uint16_t>(pack_bf16x2(sum, 0.f) & 0xFFFFu);
@@ -626,12 +646,7 @@ __global__ void __launch_bounds__(512) moe_ep_combine(const MoeArgs a, const Moe
   // 1. this rank's partials, to each column's owner
   for (int64_t e = tid; e < T * H; e += stride) {
     const int64_t t = e / H, h = e - t * H;
-    float sum = 0.f;
-    for (int j = 0; j < a.topk; ++j) {
-      const int pair = static_cast<int>(t) * a.topk + j;
-      const int ex = a.ids[pair] - a.e0;
-      if (ex >= 0 && ex < a.E_local) sum += part[static_cast<int64_t>(pair) * H + h];
-    }
+    const float sum = moe_local_slot_sum(a, part, t, h);
     const int q = static_cast<int>(h / Hs);
     st_unit_sys(ep.peers[q] + slot_off + ((static_cast<int64_t>(ep.rank) * ep.max_tokens + t) * Hs + (h - q * Hs)) * 8,
                 hi | __float_as_uint(sum));
