@@ -606,7 +606,9 @@ def run_spiral(args):
         if sp.device_status() != 0:
             raise SystemExit(f"rank {rank}: a device-side wait gave up during the parity check")
 
-    graph_steps = copies if copies <= 64 else 64
+    # whole weight-rotation cycles, at least 32 steps (128 launches) per graph:
+    # a graph boundary costs the next launch its overlap with the previous one
+    graph_steps = copies * max(1, math.ceil(32 / copies)) if copies <= 64 else 64
     timer = Timer(dev, world, graph_steps, stream)
     warm = max(3, args.warmup)
     with ClockSampler(local) as clk:
