@@ -635,7 +635,7 @@ def run_spiral(args):
 
         nk = max(graph_steps, args.steps // 4)
         launch_s = timer.timed(nk, 3, sweep_local) / nk * 1e-3 / len(BATCHES)
-    head_roof = roofline("hbm", alg, launch_s, hbm_peak, peak_kind, f"gemv_kernel<{args.fmt}>",
+    head_roof = roofline("hbm", alg, launch_s, hbm_peak, peak_kind, f"gemv_xs_kernel<{args.fmt}>",
                          profile_traffic(f"gemv_{args.fmt}_K{K}_N{Nr}_sweep"))
 
     # e2e through the public C-ABI with host buffers (pinned), copies in the
@@ -819,7 +819,7 @@ def bench_dequant(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_ki
         tot = Nt * (rb + 2 * K)
         out[f"{name}_{Nt}x{K}"] = {
             "us": t * 1e6, "GBps": tot / t / 1e9, "rows_per_rank": Nd,
-            "roofline": roofline("hbm", in_b + out_b, t, hbm_peak, peak_kind, f"dequant_rows_fast<{name}>",
+            "roofline": roofline("hbm", in_b + out_b, t, hbm_peak, peak_kind, f"dequant_rows_unit<{name}>" if name == "q6_k" else f"dequant_rows_pipe<{name}>",
                                  profile_traffic(f"dequant_{name}_K{K}_N{Nd}")),
             "l2": f"{copies} rotating input/output pairs ({copies * (in_b + out_b) / 2**20:.0f} MiB > L2)"}
         del srcs, dsts
@@ -966,7 +966,8 @@ def bench_moe(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_kind, 
         alg = ul_mean * MOE_BYTES_PER_EXPERT + T * H * 4
         res[f"T{T}"] = {"us": t * 1e6, "unique_experts": u_mean, "unique_experts_per_rank": ul_mean,
                         "weight_GBps": wbytes / t / 1e9,
-                        "roofline": roofline("hbm", alg, t, hbm_peak, peak_kind, "moe layer (4 kernels)"
+                        "roofline": roofline("hbm", alg, t, hbm_peak, peak_kind, ("moe layer: gate/up, down, combine" if T * topk <= 16 else
+                                              "moe layer: route, gate/up, down, combine")
                                              if world == 1 else "moe layer, combine fused over NVLink",
                                              profile_traffic(f"moe_T{T}_E{El}"))}
     del wg, wu, wd
@@ -1006,7 +1007,7 @@ def bench_extras(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, tc_peak,
                 alg = rb * N + B * K * 2 + B * N * 2
                 out["gemv"][f"{name}_B{B}"] = {
                     "us": t * 1e6, "weight_GBps": rb * N / t / 1e9,
-                    "roofline": roofline("hbm", alg, t, hbm_peak, peak_kind, f"gemv_kernel<{name}>",
+                    "roofline": roofline("hbm", alg, t, hbm_peak, peak_kind, f"gemv_xs_kernel<{name}>",
                                          profile_traffic(f"gemv_{name}_K{K}_N{N}_B{B}"))}
             del ws, w0
         # model shape (Gemma-style Q6_K output head, K = 1536, 262,144 rows:
@@ -1049,7 +1050,7 @@ def bench_extras(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, tc_peak,
                 alg = rbe * Ne + B * Ke * 2 + B * Ne * 2
                 out["gemv"][f"q4_0_K{Ke}_N{Ne}_B{B}"] = {
                     "us": t * 1e6, "weight_GBps": rbe * Ne / t / 1e9,
-                    "roofline": roofline("hbm", alg, t, hbm_peak, peak_kind, "gemv<q4_0> (Gemma 4 E2B shape)",
+                    "roofline": roofline("hbm", alg, t, hbm_peak, peak_kind, "gemv_xs_kernel<q4_0> (Gemma 4 E2B shape)",
                                          profile_traffic(f"gemv_q4_0_K{Ke}_N{Ne}_B{B}"))}
             del ws, w0
     out["dequant"] = bench_dequant(sp, F, dev, rank, world, timer, graph_steps, hbm_peak, peak_kind)
