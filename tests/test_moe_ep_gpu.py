@@ -7,7 +7,8 @@
 * world = 2 with the second rank absent: the owner's bounded wait for the
   missing partials gives up after 2 s, sets bit 8 of the device status and
   ends the kernel, leaving the context usable.  Nothing faults or hangs: the
-  wait is the kernel's own bounded poll of a flag that nothing sets.
+  wait is the kernel's own bounded poll of a flag that nothing sets; after
+  spiral_moe_ep_exchange_reset the exchange serves a world = 1 call again.
 The multi-rank combine itself is checked on 2+ GPUs in tests/test_multi_gpu.py.
 """
 
@@ -85,4 +86,15 @@ def test_moe_ep_absent_rank_times_out_and_reports(cuda):
     y = sp.moe_ffn(fid, wg, wu, wd, x, ids, w, hidden=H, inter=I, n_experts_local=E)
     torch.cuda.synchronize()
     assert torch.isfinite(y.float()).all()
+    assert sp.device_status() == 0
+    # recovery: the zeroed exchange runs the protocol from its start (world 1)
+    assert bool(own.any())
+    sp.moe_ep_exchange_reset(own, H, max_tokens)
+    torch.cuda.synchronize()
+    assert not bool(own.any())
+    solo = torch.tensor([own.data_ptr()], dtype=torch.int64, device="cuda")
+    got = sp.moe_ffn_ep(fid, wg, wu, wd, x, ids, w, hidden=H, inter=I, n_experts_local=E, expert_first=0,
+                        exchange_peers_dev=solo, rank=0, world=1, max_tokens=max_tokens)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), y.view(torch.int16))
     assert sp.device_status() == 0

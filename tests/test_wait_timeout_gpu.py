@@ -72,11 +72,20 @@ def test_gathered_wait_gives_up_and_reports_timeout(cuda):
     got = y[:, :N_shard].float().cpu().numpy()
     ok, rel = tolerance_ok(got, ref, bf16_out=True)
     assert ok, rel
-    # recovery: the exchange (call count, flags, pieces) is zeroed again
+    # recovery: the exchange (call count, flags, pieces) is zeroed again, and
+    # a call on it runs the protocol from its start (world 1: this rank
+    # alone), equal bit for bit to the plain MUL_MAT
     assert bool(own.any())
     sp.allgather_exchange_reset(own, N_total)
     torch.cuda.synchronize()
     assert not bool(own.any())
+    w_full = dev_bytes(raw)
+    solo = torch.tensor([own.data_ptr()], dtype=torch.int64, device="cuda")
+    yg = torch.zeros((M, N_total), dtype=torch.bfloat16, device="cuda")
+    sp.mul_mat_allgather(fid, w_full, xd, N_total, K, yg, 0, solo, 0, 1)
+    want = sp.mul_mat(fid, w_full, xd, N_total, K, y_dtype=sp.BF16)
+    assert torch.equal(yg.view(torch.int16), want.view(torch.int16))
+    assert sp.device_status() == 0
     # the context is still usable: an ordinary MUL_MAT right after
     y2 = sp.mul_mat(fid, w_shard, xd, N_shard, K, y_dtype=sp.F32).cpu().numpy()
     ok, rel = tolerance_ok(y2, ref, bf16_out=False)
