@@ -29,6 +29,12 @@
  * spiral_status.  Size queries and the repack return 0 on invalid input,
  * exactly like the reference's record_count / packed_bytes / repack_weights
  * (src/quants/q4_0/repack.h:10-41, TODO.md:331-334).  Nothing throws or traps.
+ *
+ * Per-device state: the first call on a device sets the kernels' shared-memory
+ * limits and caches the device's SM count and attributes (and, for
+ * spiral_moe_ffn_noalloc, its scratch address) for the process.  None of it
+ * survives cudaDeviceReset or any other reset of the device's primary
+ * context: after one, load the library into a new process before calling it.
  */
 #ifndef SPIRAL_B200_H
 #define SPIRAL_B200_H
